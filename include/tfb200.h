@@ -1,0 +1,133 @@
+/*
+ * tfb200.h - C ABI of the B200 (sm_100a) kernels behind
+ * transformer_optimization_b200.UserOptimizedTransformer.
+ *
+ * The reference (namsengi11/transformer_optimization) has no native code and
+ * no FFI: its hot path, UserOptimizedTransformer.forward
+ * (torch_transformer_benchmark.py:3509-3611, per-layer schedule 4003-4326),
+ * calls Triton kernels and ATen through Python wrappers. Each entry point
+ * below replaces one of those wrappers; the comment on each names it.
+ *
+ * Conventions
+ *   - Plain device pointers, element counts/strides in ELEMENTS, int64 sizes.
+ *   - `stream` is a cudaStream_t (CUstream) passed as void*; NULL = legacy
+ *     default stream. Every call only enqueues work: no host synchronisation,
+ *     no device allocation (all buffers are caller-owned), safe inside CUDA
+ *     graph capture once the same call has run once on the device.
+ *   - Return 0 (TF_OK) or a TF_ERR_* code; tf_last_error() gives the message.
+ *     Kernels never trap: a pipeline wait that exceeds its time bound writes a
+ *     code into the device status word (read with tf_device_status) and the
+ *     kernel returns.
+ *   - fp16 = IEEE binary16 ("half"), fp32 = binary32.
+ */
+#ifndef TFB200_H
+#define TFB200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes */
+#define TF_OK 0
+#define TF_ERR_SHAPE 1       /* unsupported or inconsistent sizes */
+#define TF_ERR_ALIGN 2       /* pointer / stride alignment */
+#define TF_ERR_LAUNCH 3      /* CUDA launch or attribute error */
+#define TF_ERR_UNSUPPORTED 4 /* device is not sm_100 */
+#define TF_ERR_DEVICE 5      /* CUDA runtime error outside a launch */
+#define TF_ERR_DRIVER 6      /* driver entry point (tensor-map encode) */
+#define TF_ERR_TIMEOUT 7     /* a kernel wait ran out (see tf_device_status) */
+
+/* tf_ln_residual flags */
+#define TF_LN_MASK_DELTA 1 /* zero invalid rows of delta before the add */
+#define TF_LN_MASK_X 2     /* zero invalid rows of x after the add */
+#define TF_LN_MASK_OUT 4   /* zero invalid rows of the normalised output */
+#define TF_LN_WRITE_X 8    /* store the updated residual into x_out */
+#define TF_LN_OUT_F32 16   /* normed is fp32 (default fp16) */
+
+/* tf_gemm epilogues */
+#define TF_EPI_BIAS 0      /* C = fp16(acc + bias) */
+#define TF_EPI_BIAS_GELU 1 /* C = fp16(gelu_erf(fp16(acc + bias))) */
+
+/* tf_flash_fwd flags */
+#define TF_ATTN_CAUSAL 1  /* mask key position > query position */
+#define TF_ATTN_OUT_F32 2 /* out is fp32 (default fp16) */
+
+/* ABI version, bumped on any signature change. */
+int tf_abi_version(void);
+
+/* Message of the last failed call on this host thread ("" if none). */
+const char* tf_last_error(void);
+
+/* Synchronises `stream`, then returns the device status word of the current
+ * device in *code (0 = no kernel wait ran out) and clears it.
+ * No reference counterpart: the reference's Triton wrappers raise
+ * (torch_transformer_benchmark.py:1053-1058) and cannot time out. */
+int tf_device_status(int* code, void* stream);
+
+/* One residual-add + LayerNorm site over a contiguous [M, D] activation:
+ *   x_new  = mask_x(x + mask_delta(fp32(delta)))
+ *   normed = mask_out(LayerNorm(x_new) * w + b)       (fp16 or fp32 store)
+ * delta is fp16 [M, D] or NULL (no add); valid is uint8 [M] (nonzero = valid
+ * token) or NULL when no mask flag is set; x_out may alias nothing else and
+ * is written only with TF_LN_WRITE_X. D must be a multiple of 8, <= 4096.
+ * Replaces _ln_site / _triton_add_layernorm / _add_ln_kernel
+ * (torch_transformer_benchmark.py:3940-4001, 1038-1108, 884-962). */
+int tf_ln_residual(const float* x, const void* delta, const float* w, const float* b, float eps,
+                   const uint8_t* valid, int64_t M, int64_t D, int flags, float* x_out, void* normed,
+                   void* stream);
+
+/* fp16 GEMM, fp32 accumulation on tcgen05 tensor cores:
+ *   C[M, N] = epilogue(A[M, K] * W[N, K]^T + bias[N])
+ * A row-major with pitch lda, W = nn.Linear weight [N, K] with pitch ldw,
+ * C row-major with pitch ldc; all fp16. N % 32 == 0, K and pitches % 8 == 0,
+ * pointers 16-byte aligned.
+ * Replaces _lin / _triton_linear / _triton_gemm_gelu / F.linear on the
+ * fp16-GEMM path (torch_transformer_benchmark.py:4138-4194, 1860-1906,
+ * kernel 1756-1803). */
+int tf_gemm(const void* A, int64_t lda, const void* W, int64_t ldw, const void* bias, void* C, int64_t ldc,
+            int64_t M, int64_t N, int64_t K, int epilogue, void* stream);
+
+/* tf_gemm with an explicit N tile (64, 128 or 256; 0 = automatic). For
+ * tuning and tests. */
+int tf_gemm_tiled(const void* A, int64_t lda, const void* W, int64_t ldw, const void* bias, void* C,
+                  int64_t ldc, int64_t M, int64_t N, int64_t K, int epilogue, int tile_n, void* stream);
+
+/* Flash attention forward (online softmax, no score matrix in HBM):
+ *   out[b, i, h*hd:(h+1)*hd] = sum_j softmax_j(scale * q_i . k_j) v_j
+ * q: fp16, token i of batch b, head h at q + b*bs_q + i*ld_q + h*hd;
+ * k, v: same with ld_kv / bs_kv over seq_k tokens; out: fp16 (or fp32 with
+ * TF_ATTN_OUT_F32) with ld_o / bs_o. lse: fp32 [batch, heads, seq_q] natural
+ * log-sum-exp of the scaled scores per row, or NULL. key_valid: uint8
+ * [batch, seq_k] (nonzero = key may be attended) or NULL. With
+ * TF_ATTN_CAUSAL key j is masked when k_pos0 + j > q_pos0 + i (positions
+ * are global token indices, for context-parallel blocks). A row with no
+ * admissible key gets out = 0 and lse = -inf. head_dim 64 or 128.
+ * Replaces F.scaled_dot_product_attention / _triton_short_attention /
+ * _flash_attn_kernel on the fp16 path (torch_transformer_benchmark.py:
+ * 4146-4161, 1306-1418, 1193-1304). */
+int tf_flash_fwd(const void* q, const void* k, const void* v, int64_t ld_q, int64_t ld_kv, int64_t bs_q,
+                 int64_t bs_kv, void* out, int64_t ld_o, int64_t bs_o, float* lse, const uint8_t* key_valid,
+                 int64_t batch, int64_t heads, int64_t seq_q, int64_t seq_k, int64_t head_dim, float scale,
+                 int64_t q_pos0, int64_t k_pos0, int flags, void* stream);
+
+/* Merge one partial attention result into a running one (log-sum-exp
+ * combination, exact): with L = logaddexp(lse_acc, lse_part)
+ *   o_acc   = o_acc * exp(lse_acc - L) + o_part * exp(lse_part - L)
+ *   lse_acc = L
+ * o_acc, o_part: fp32 [batch, seq_q, heads*head_dim] with pitch ld (tokens)
+ * and bs (batches); lse_*: fp32 [batch, heads, seq_q]. If out16 is not NULL
+ * the merged result is also written there as fp16 (pitch ld16, bs16).
+ * No reference counterpart: the reference has no context parallelism; this
+ * is the combine step of the ring attention that replaces its capacity
+ * streaming (torch_transformer_benchmark.py:4686-4771, 4933-5013). */
+int tf_attn_merge(float* o_acc, float* lse_acc, const float* o_part, const float* lse_part, int64_t ld,
+                  int64_t bs, void* out16, int64_t ld16, int64_t bs16, int64_t batch, int64_t heads,
+                  int64_t seq_q, int64_t head_dim, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TFB200_H */

@@ -1,0 +1,217 @@
+"""Kernel-level parity on a B200: each CUDA kernel against the oracle's
+statement of the same op (oracle/reference_model.py), on seeded inputs,
+through the C ABI (transformer_optimization_b200.kernels -> libtfb200.so).
+
+Tolerances (written per test):
+* LayerNorm: fp32 math, different reduction tree -> 2e-5 abs on fp32 output,
+  1 fp16 ulp on fp16 output.
+* GEMM: fp16 output of an fp32-accumulated sum; the reference value is the
+  exact (fp64) sum rounded to fp16, so the kernel may differ by one fp16 ulp
+  where the fp32 accumulation order tips a rounding: |d| <= 2e-3*|ref| + 1e-3.
+* Attention: P is rounded to fp16 before the PV product (as the reference's
+  fp16 SDPA path does): |d| <= 1e-2*|ref| + 3e-3 on fp16 outputs, LSE 2e-3.
+"""
+
+import math
+
+import pytest
+import torch
+
+from oracle import reference_model as om
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def K():
+    from transformer_optimization_b200 import _abi, kernels
+    _abi.load()
+    torch.backends.cuda.matmul.allow_tf32 = False
+    yield kernels
+    assert _abi.device_status() == 0, "a kernel wait ran out"
+
+
+def _dev():
+    return torch.device("cuda:0")
+
+
+# ----------------------------------------------------------------- LayerNorm
+@pytest.mark.parametrize("m,d", [(1, 256), (7, 64), (64, 512), (1000, 1024), (333, 2048), (40, 4096), (5, 136)])
+@pytest.mark.parametrize("flags", ["plain", "delta", "mask_delta", "mask_x", "final"])
+def test_ln_residual(K, m, d, flags):
+    g = torch.Generator().manual_seed(m * 31 + d)
+    x = torch.randn(m, d, generator=g) * 2 + 0.5
+    delta = (torch.randn(m, d, generator=g) * 0.5).half()
+    w = torch.randn(d, generator=g) * 0.1 + 1
+    b = torch.randn(d, generator=g) * 0.1
+    valid = torch.rand(m, generator=g) > 0.3
+    use_delta = flags != "plain"
+    md, mx, mo = flags == "mask_delta", flags in ("mask_x", "final"), flags == "final"
+    out_f32 = flags == "final"
+    xr, yr = om.ln_site(x, delta if use_delta else None, w, b, 1e-5, valid, md, mx, mo)
+    dv = _dev()
+    xg = x.to(dv)
+    x_new, y = K.ln_residual(xg, delta.to(dv) if use_delta else None, w.to(dv), b.to(dv), 1e-5,
+                             valid.to(dv), mask_delta=md, mask_x=mx, mask_out=mo, write_x=use_delta,
+                             out_dtype=torch.float32 if out_f32 else torch.float16)
+    torch.cuda.synchronize()
+    if use_delta:
+        assert torch.allclose(x_new.cpu(), xr, atol=0, rtol=0)  # same fp32 add
+    if out_f32:
+        assert torch.allclose(y.cpu(), yr, atol=2e-5, rtol=1e-5)
+    else:
+        assert torch.allclose(y.float().cpu(), yr.half().float(), atol=2e-3, rtol=1e-3)
+
+
+def test_ln_residual_in_place(K):
+    g = torch.Generator().manual_seed(5)
+    x = torch.randn(300, 1024, generator=g)
+    delta = torch.randn(300, 1024, generator=g).half()
+    w, b = torch.ones(1024), torch.zeros(1024)
+    xr, yr = om.ln_site(x, delta, w, b, 1e-5, None, False, False, False)
+    xg = x.cuda()
+    K.ln_residual(xg, delta.cuda(), w.cuda(), b.cuda(), 1e-5, write_x=True, x_out=xg)
+    assert torch.equal(xg.cpu(), xr)
+
+
+# ----------------------------------------------------------------- GEMM
+GEMM_SHAPES = [  # (M, K, N): model projections at small M plus ragged rows
+    (256, 256, 768), (256, 256, 1024), (256, 1024, 256), (64, 512, 1536), (64, 2048, 512),
+    (300, 1024, 3072), (1000, 1024, 4096), (129, 4096, 1024), (2048, 2048, 6144), (17, 64, 64),
+]
+
+
+@pytest.mark.parametrize("m,k,n", GEMM_SHAPES)
+@pytest.mark.parametrize("gelu", [False, True])
+def test_gemm(K, m, k, n, gelu):
+    g = torch.Generator().manual_seed(m + 7 * k + 13 * n)
+    a = torch.randn(m, k, generator=g).half()
+    bound = 1 / math.sqrt(k)
+    w = (torch.rand(n, k, generator=g) * 2 - 1).mul(bound).half()
+    bias = (torch.rand(n, generator=g) * 2 - 1).mul(bound).half()
+    ref = om.linear_fp16(a, w, bias, gelu)
+    out = K.linear(a.cuda(), w.cuda(), bias.cuda(), gelu=gelu).float().cpu()
+    err = (out - ref).abs()
+    assert torch.all(err <= 2e-3 * ref.abs() + 1e-3), f"max err {err.max()}"
+
+
+@pytest.mark.parametrize("tile_n", [64, 128, 256])
+def test_gemm_tiles(K, tile_n):
+    m, k, n = 777, 1024, 1536
+    g = torch.Generator().manual_seed(tile_n)
+    a = torch.randn(m, k, generator=g).half()
+    w = (torch.randn(n, k, generator=g) / 32).half()
+    bias = torch.randn(n, generator=g).half()
+    ref = om.linear_fp16(a, w, bias, False)
+    out = K.linear(a.cuda(), w.cuda(), bias.cuda(), tile_n=tile_n).float().cpu()
+    assert torch.all((out - ref).abs() <= 2e-3 * ref.abs() + 1e-3)
+
+
+def test_gemm_strided_output(K):
+    """QKV-style: write into a column slice of a wider buffer."""
+    m, k, n = 200, 512, 512
+    a = torch.randn(m, k).half().cuda()
+    w = (torch.randn(n, k) / 23).half().cuda()
+    bias = torch.zeros(n).half().cuda()
+    big = torch.zeros(m, 3 * n, dtype=torch.float16, device="cuda")
+    K.linear(a, w, bias, out=big[:, n:2 * n])
+    ref = om.linear_fp16(a.cpu(), w.cpu(), bias.cpu(), False)
+    assert torch.all(((big[:, n:2 * n].float().cpu()) - ref).abs() <= 2e-3 * ref.abs() + 1e-3)
+    assert torch.count_nonzero(big[:, :n]) == 0 and torch.count_nonzero(big[:, 2 * n:]) == 0
+
+
+# ----------------------------------------------------------------- attention
+ATTN_CASES = [  # (B, H, Sq, Sk, hd, causal, masked)
+    (2, 4, 128, 128, 64, False, False),
+    (2, 4, 128, 128, 64, True, False),
+    (1, 8, 64, 64, 64, False, False),
+    (1, 2, 300, 300, 128, False, False),
+    (1, 2, 300, 300, 128, True, False),
+    (3, 2, 200, 200, 64, False, True),
+    (2, 3, 257, 257, 64, True, True),
+    (1, 2, 1000, 1000, 128, True, False),
+    (2, 16, 512, 512, 64, False, False),
+]
+
+
+def _qkv(b, h, s, hd, seed):
+    g = torch.Generator().manual_seed(seed)
+    qkv = (torch.randn(b, s, 3 * h * hd, generator=g) * 1.5).half()
+    return qkv
+
+
+@pytest.mark.parametrize("b,h,sq,sk,hd,causal,masked", ATTN_CASES)
+def test_flash_packed_qkv(K, b, h, sq, sk, hd, causal, masked):
+    d = h * hd
+    qkv = _qkv(b, h, sq, hd, sq + hd)
+    kv_valid = None
+    if masked:
+        kv_valid = torch.arange(sk)[None, :] < torch.randint(1, sk + 1, (b,), generator=torch.Generator().manual_seed(1))[:, None]
+    q = qkv[..., :d].reshape(b, sq, h, hd).transpose(1, 2)
+    k = qkv[..., d:2 * d].reshape(b, sk, h, hd).transpose(1, 2)
+    v = qkv[..., 2 * d:].reshape(b, sk, h, hd).transpose(1, 2)
+    ref, lse_ref = om.attention_fp16(q, k, v, hd ** -0.5, causal, kv_valid)
+    ref = ref.transpose(1, 2).reshape(b, sq, d)
+    g = qkv.cuda()
+    out, lse = K.flash_attention(g[..., :d], g[..., d:2 * d], g[..., 2 * d:], h, hd ** -0.5, causal=causal,
+                                 key_valid=None if kv_valid is None else kv_valid.cuda(), want_lse=True)
+    out = out.float().cpu()
+    err = (out - ref).abs()
+    assert torch.all(err <= 1e-2 * ref.abs() + 3e-3), f"max err {err.max()}"
+    lse = lse.cpu()
+    fin = torch.isfinite(lse_ref)
+    assert torch.equal(fin, torch.isfinite(lse))
+    assert torch.allclose(lse[fin], lse_ref[fin], atol=2e-3, rtol=1e-4)
+
+
+@pytest.mark.parametrize("hd", [64, 128])
+def test_flash_offsets_and_f32_out(K, hd):
+    """Context-parallel block: queries at global positions [q0, q0+Sq), keys
+    at [k0, k0+Sk); causal mask on global positions; fp32 output."""
+    b, h, sq, sk = 1, 2, 200, 300
+    q0, k0 = 500, 380
+    g = torch.Generator().manual_seed(hd)
+    q = (torch.randn(b, sq, h * hd, generator=g)).half()
+    kk = (torch.randn(b, sk, h * hd, generator=g)).half()
+    vv = (torch.randn(b, sk, h * hd, generator=g)).half()
+    split = lambda t, s: t.reshape(b, s, h, hd).transpose(1, 2)
+    ref, lse_ref = om.attention_fp16(split(q, sq), split(kk, sk), split(vv, sk), hd ** -0.5, True, None,
+                                     q_offset=q0 - k0)
+    ref = ref.transpose(1, 2).reshape(b, sq, h * hd)
+    out, lse = K.flash_attention(q.cuda(), kk.cuda(), vv.cuda(), h, hd ** -0.5, causal=True, q_pos0=q0,
+                                 k_pos0=k0, out_dtype=torch.float32, want_lse=True)
+    out = out.cpu()
+    assert torch.all((out - ref).abs() <= 1e-2 * ref.abs() + 3e-3)
+    fin = torch.isfinite(lse_ref)
+    assert torch.equal(fin, torch.isfinite(lse.cpu()))
+    assert torch.allclose(lse.cpu()[fin], lse_ref[fin], atol=2e-3)
+
+
+def test_flash_fully_masked_rows(K):
+    """Queries before every key (causal) get out = 0 and lse = -inf."""
+    b, h, hd, sq, sk = 1, 1, 64, 130, 128
+    q = torch.randn(b, sq, hd).half().cuda()
+    k = torch.randn(b, sk, hd).half().cuda()
+    out, lse = K.flash_attention(q, k, k, h, 0.125, causal=True, q_pos0=0, k_pos0=1000, want_lse=True)
+    assert torch.count_nonzero(out) == 0
+    assert torch.all(torch.isneginf(lse))
+
+
+def test_attn_merge(K):
+    b, s, h, hd = 2, 100, 4, 64
+    g = torch.Generator().manual_seed(3)
+    oa = torch.randn(b, s, h * hd, generator=g)
+    ob = torch.randn(b, s, h * hd, generator=g)
+    la = torch.randn(b, h, s, generator=g)
+    lb = torch.randn(b, h, s, generator=g)
+    la[0, 0, :5] = -math.inf
+    L = torch.logaddexp(la, lb)
+    wa = torch.exp(la - L).transpose(1, 2).repeat_interleave(hd, dim=2)
+    wb = torch.exp(lb - L).transpose(1, 2).repeat_interleave(hd, dim=2)
+    ref = oa * wa + ob * wb
+    oag, lag = oa.cuda(), la.cuda()
+    o16 = torch.empty(b, s, h * hd, dtype=torch.float16, device="cuda")
+    K.attn_merge(oag, lag, ob.cuda(), lb.cuda(), h, out16=o16)
+    assert torch.allclose(oag.cpu(), ref, atol=1e-5, rtol=1e-5)
+    assert torch.allclose(lag.cpu(), L, atol=1e-5)
+    assert torch.allclose(o16.float().cpu(), ref, atol=2e-3, rtol=1e-3)

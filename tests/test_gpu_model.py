@@ -1,0 +1,148 @@
+"""End-to-end parity on a B200: UserOptimizedTransformer (sm_100a kernels via
+the C ABI) against the oracle's fp32 eager model on identical seeded weights
+and inputs, judged by the reference's own gate (compare_outputs,
+torch_transformer_benchmark.py:4548-4615): |d| <= 0.002 OR |d| <= 0.02*|ref|
+with ZERO failing elements.
+
+Small configs run the oracle on the CPU. c3-c5 run the same oracle code on
+the GPU in strict fp32 (TF32 off); c4/c5 use its query-tiled attention and
+row-chunked FFN (the reference's QueryTiledBaselineTransformer arithmetic)
+to bound memory.
+"""
+
+import pytest
+import torch
+
+from oracle import reference_model as om
+from transformer_optimization_b200 import NAMED_CONFIGS, TransformerConfig, UserOptimizedTransformer
+from transformer_optimization_b200._abi import TfError
+
+pytestmark = pytest.mark.gpu
+ATOL, RTOL = 0.002, 0.02
+
+
+def _build(cfg, seed=0):
+    p, x = om.seeded_case(cfg, seed)
+    model = UserOptimizedTransformer(cfg)
+    model.load_state_dict(p, strict=True)
+    return p, x, model.cuda().eval()
+
+
+def _check(ref, out):
+    r = om.compare_outputs(ref.float().cpu(), out.float().cpu(), rtol=RTOL, atol=ATOL)
+    assert r.passed, (f"{r.failed_elements}/{r.total_elements} failed, max_abs={r.max_abs_error:.3g} "
+                      f"at {r.worst_index} ref={r.reference_at_worst:.6g} opt={r.optimized_at_worst:.6g}")
+    return r
+
+
+SMALL = {
+    "c1": NAMED_CONFIGS["c1"],
+    "c1_causal": TransformerConfig(2, 128, 256, 4, 1024, 2, True),
+    "c2": NAMED_CONFIGS["c2"],
+    "c2_causal": TransformerConfig(1, 64, 512, 8, 2048, 6, True),
+    "ragged_hd128": TransformerConfig(1, 100, 256, 2, 512, 1, False),
+    "ragged_causal": TransformerConfig(3, 300, 128, 2, 256, 2, True),
+    "d2048_hd128": TransformerConfig(2, 256, 2048, 16, 8192, 2, False),
+}
+
+
+@pytest.mark.parametrize("name", sorted(SMALL))
+def test_small_configs(name):
+    cfg = SMALL[name]
+    p, x, model = _build(cfg)
+    ref = om.forward(p, cfg, x)
+    with torch.inference_mode():
+        out = model(x.cuda())
+    _check(ref, out)
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_partial_mask(causal):
+    cfg = TransformerConfig(3, 200, 256, 4, 1024, 2, causal)
+    p, x, model = _build(cfg, seed=7)
+    mask = om.padded_mask(cfg, 0.4, 1007)
+    x = x.masked_fill(~mask[..., None], 0)
+    ref = om.forward(p, cfg, x, mask)
+    with torch.inference_mode():
+        out = model(x.cuda(), mask.cuda())
+    _check(ref, out)
+    assert torch.count_nonzero(out.cpu()[~mask]) == 0
+
+
+def test_all_true_mask_and_graph_replay():
+    """The harness always passes an all-True mask (torch_transformer_benchmark.py:
+    4380-4384). Replays are bit-identical, the input is not mutated and the
+    output does not alias the graph's static buffer."""
+    cfg = NAMED_CONFIGS["c2"]
+    p, x, model = _build(cfg)
+    xg = x.cuda()
+    x_copy = xg.clone()
+    mask = torch.ones(1, 64, dtype=torch.bool, device="cuda")
+    with torch.inference_mode():
+        a = model(xg, mask)
+        b = model(xg, mask)
+        c = model(xg)
+    assert torch.equal(xg, x_copy)
+    assert torch.equal(a, b) and torch.equal(a, c)
+    assert a.data_ptr() != b.data_ptr()
+    assert len(model._graph_cache) == 2  # all_true and none keys
+    model.use_cuda_graphs = False
+    with torch.inference_mode():
+        e = model(xg)
+    assert torch.equal(a, e)  # graph replay == the same kernels run eagerly
+    _check(om.forward(p, cfg, x), a)
+
+
+def test_weight_reload_invalidates_caches():
+    cfg = NAMED_CONFIGS["c1"]
+    p, x, model = _build(cfg)
+    with torch.inference_mode():
+        a = model(x.cuda())
+    p2, _ = om.seeded_case(cfg, 1)
+    model.load_state_dict(p2)
+    with torch.inference_mode():
+        b = model(x.cuda())
+    _check(om.forward(p2, cfg, x), b)
+    assert not torch.equal(a, b)
+
+
+def test_errors_are_loud():
+    cfg = TransformerConfig(1, 64, 128, 4, 256, 1, False)  # head_dim 32: no kernel
+    model = UserOptimizedTransformer(cfg).cuda()
+    with pytest.raises(TfError):
+        model(torch.randn(1, 64, 128, device="cuda"))
+    with pytest.raises(RuntimeError):
+        UserOptimizedTransformer(NAMED_CONFIGS["c1"])(torch.randn(2, 128, 256))
+
+
+def _gpu_oracle(p, cfg, x, **kw):
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.backends.cudnn.allow_tf32 = False
+    pg = {k: v.cuda() for k, v in p.items()}
+    with torch.inference_mode():
+        return om.forward(pg, cfg, x.cuda(), **kw)
+
+
+@pytest.mark.parametrize("name,kw", [
+    ("c3", {}),
+    ("c4", {"query_tile": 512, "ffn_row_chunk": 32768}),
+    ("c5", {"query_tile": 1024, "ffn_row_chunk": 32768}),
+])
+def test_large_configs(name, kw):
+    cfg = NAMED_CONFIGS[name]
+    p, x, model = _build(cfg)
+    with torch.inference_mode():
+        out = model(x.cuda())
+    del model
+    ref = _gpu_oracle(p, cfg, x, **kw)
+    _check(ref, out)
+
+
+def test_c5_causal():
+    cfg = TransformerConfig(1, 100000, 1024, 16, 4096, 4, True)
+    p, x, model = _build(cfg)
+    with torch.inference_mode():
+        out = model(x.cuda())
+    del model
+    ref = _gpu_oracle(p, cfg, x, query_tile=1024, ffn_row_chunk=32768)
+    _check(ref, out)

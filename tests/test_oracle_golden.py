@@ -1,0 +1,75 @@
+"""Pin the oracle against the real reference's outputs (CPU, no GPU).
+
+`tests/golden/golden_cases.pt` was produced by `tests/golden/make_golden.py`,
+which runs the reference's own `BaselineTransformer` /
+`QueryTiledBaselineTransformer` (torch_transformer_benchmark.py:135-248,
+341-437). These tests rebuild each case with the oracle only and require:
+
+* the same weights and inputs (state_dict and x checksums),
+* the same outputs: bit-equal when this host runs the torch build that made
+  the fixtures, within 1e-5 otherwise (a different BLAS may reorder fp32 sums).
+"""
+
+from pathlib import Path
+
+import pytest
+import torch
+
+from oracle import reference_model as om
+from transformer_optimization_b200.config import TransformerConfig
+
+GOLDEN = torch.load(Path(__file__).parent / "golden" / "golden_cases.pt", weights_only=False)
+
+
+def _sd_checksum(p):
+    tot = torch.zeros((), dtype=torch.float64)
+    wsum = torch.zeros((), dtype=torch.float64)
+    for i, (k, v) in enumerate(p.items()):
+        v = v.double()
+        tot += v.sum()
+        wsum += (v.flatten()[:: max(1, v.numel() // 97)] * (i + 1)).sum()
+    return torch.stack([tot, wsum])
+
+
+@pytest.mark.parametrize("name", sorted(GOLDEN["cases"]))
+def test_oracle_matches_reference(name):
+    rec = GOLDEN["cases"][name]
+    b, s, d, h, f, l, causal, pad, qtile, seed = rec["shape"]
+    cfg = TransformerConfig(b, s, d, h, f, l, causal)
+    torch.set_num_threads(min(8, torch.get_num_threads()))
+    p, x = om.seeded_case(cfg, seed)
+    assert torch.allclose(_sd_checksum(p), rec["sd_checksum"], rtol=0, atol=1e-9), \
+        "oracle init_params does not rebuild the reference's weights"
+    mask = rec["mask"]
+    if mask is not None:
+        x = x.masked_fill(~mask[..., None], 0)
+        assert torch.equal(om.padded_mask(cfg, pad, seed + 1000), mask)
+    assert torch.allclose(torch.stack([x.double().sum(), (x.double() ** 2).sum()]),
+                          rec["x_checksum"], rtol=0, atol=1e-9)
+    with torch.inference_mode():
+        y = om.forward(p, cfg, x, mask, query_tile=qtile, ffn_row_chunk=4096 if qtile else None)
+    if rec["y_index"] is not None:
+        y = y[:, rec["y_index"], :]
+    tol = 0.0 if GOLDEN["torch_version"] == torch.__version__ else 1e-5
+    assert torch.allclose(y, rec["y"], rtol=0, atol=tol), (y - rec["y"]).abs().max()
+
+
+def test_compare_outputs_or_criterion():
+    """compare_outputs uses (abs<=atol) OR (abs<=rtol*|ref|), not isclose."""
+    ref = torch.tensor([1.0, 0.1, 0.0, float("nan")])
+    # 0.02 abs on 1.0 passes by rtol, 0.0021 abs on 0.1 fails both,
+    # 0.0019 on 0 passes by atol, NaN always fails.
+    opt = torch.tensor([1.02, 0.1021, 0.0019, 0.0])
+    r = om.compare_outputs(ref, opt, rtol=0.02, atol=0.002)
+    assert not r.passed
+    assert r.failed_elements == 2
+    r2 = om.compare_outputs(ref[:3], opt[:3].clone().index_fill_(0, torch.tensor([1]), 0.1019))
+    assert r2.passed
+
+
+def test_query_tiled_equals_dense():
+    cfg = TransformerConfig(1, 70, 64, 2, 96, 1, True)
+    p, x = om.seeded_case(cfg, 11)
+    y0 = om.forward(p, cfg, x)
+    y1 = om.forward(p, cfg, x, query_tile=16, ffn_row_chunk=33)
+    assert torch.allclose(y0, y1, atol=1e-5)

@@ -1,0 +1,75 @@
+// Host-side helpers shared by the kernel launchers: error recording, device
+// properties, the device status word and TMA tensor-map encoding.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/tfb200.h"
+
+namespace tfb {
+
+// Records a formatted message for tf_last_error() and returns `code`.
+int set_error(int code, const char* fmt, ...);
+int last_error_code();
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Streaming-multiprocessor count of the current device (cached).
+int device_sm_count();
+
+// Device address of the library's status word on the current device
+// (resolved once per device); nullptr after recording an error.
+int* device_status_ptr();
+
+// 2-D fp16 tensor map, 128-byte swizzle: inner extent `inner` elements with
+// row pitch `ld` elements, `outer` rows, box of box_inner x box_outer.
+int make_tmap_2d_f16(CUtensorMap* map, const void* base, long long inner, long long outer, long long ld,
+                     int box_inner, int box_outer);
+
+// 3-D fp16 tensor map (inner, rows, batches) with row pitch `ld` and batch
+// pitch `bstride` (elements), 128-byte swizzle, box box_inner x box_rows x 1.
+int make_tmap_3d_f16(CUtensorMap* map, const void* base, long long inner, long long rows, long long batches,
+                     long long ld, long long bstride, int box_inner, int box_rows);
+
+// kernels (defined in their own translation units)
+int gemm_f16(const void* A, long long lda, const void* W, long long ldw, const void* bias, void* C,
+             long long ldc, long long M, long long N, long long K, int epilogue, int force_bn,
+             cudaStream_t stream);
+
+int ln_residual(const float* x, const void* delta, const float* w, const float* b, float eps,
+                const uint8_t* valid, long long M, int D, int flags, float* x_out, void* normed,
+                cudaStream_t stream);
+
+struct AttnArgs {
+  const void* q;
+  const void* k;
+  const void* v;
+  long long ld_q, ld_kv, bs_q, bs_kv;
+  void* out;
+  long long ld_o, bs_o;
+  float* lse;
+  const uint8_t* key_valid;
+  long long batch, heads, seq_q, seq_k, head_dim;
+  float scale;
+  long long q_pos0, k_pos0;
+  int flags;
+};
+
+int flash_fwd(const AttnArgs& a, cudaStream_t stream);
+
+struct MergeArgs {
+  float* o_acc;
+  float* lse_acc;
+  const float* o_part;
+  const float* lse_part;
+  long long ld, bs;
+  void* out16;
+  long long ld16, bs16;
+  long long batch, heads, seq_q, head_dim;
+};
+
+int attn_merge(const MergeArgs& a, cudaStream_t stream);
+
+}  // namespace tfb

@@ -1,0 +1,158 @@
+"""Tensor-level wrappers over the C ABI (one per exported kernel).
+
+Each wrapper checks dtypes, devices and strides, allocates its output when
+the caller gives none, and enqueues the kernel on the current CUDA stream
+(so it can be captured in a CUDA graph). None of them has a fallback: a
+tensor on the CPU, a wrong dtype or a missing library raises.
+"""
+
+from __future__ import annotations
+
+from typing import Optional, Tuple
+
+import torch
+
+from . import _abi
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _need_cuda(name: str, *ts: Optional[torch.Tensor]) -> None:
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError(f"{name}: every operand must be a CUDA tensor (no CPU path)")
+
+
+def ln_residual(x: torch.Tensor, delta: Optional[torch.Tensor], weight: torch.Tensor, bias: torch.Tensor,
+                eps: float, valid: Optional[torch.Tensor] = None, *, mask_delta: bool = False,
+                mask_x: bool = False, mask_out: bool = False, write_x: bool = False,
+                x_out: Optional[torch.Tensor] = None, out_dtype: torch.dtype = torch.float16,
+                normed: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+    """One residual site (tf_ln_residual). x: fp32 [..., D] contiguous; delta:
+    fp16 of the same shape or None; valid: bool/uint8 [rows] or None.
+    Returns (x_new, normed); x_new is x_out (may be x itself: the kernel reads
+    each row fully before writing it) when write_x, else x."""
+    _need_cuda("ln_residual", x, delta, weight, bias, valid, x_out, normed)
+    if x.dtype != torch.float32 or not x.is_contiguous():
+        raise ValueError("ln_residual: x must be contiguous fp32")
+    d = x.shape[-1]
+    m = x.numel() // d
+    if delta is not None and (delta.dtype != torch.float16 or not delta.is_contiguous() or delta.numel() != x.numel()):
+        raise ValueError("ln_residual: delta must be contiguous fp16 shaped like x")
+    flags = 0
+    if mask_delta:
+        flags |= _abi.TF_LN_MASK_DELTA
+    if mask_x:
+        flags |= _abi.TF_LN_MASK_X
+    if mask_out:
+        flags |= _abi.TF_LN_MASK_OUT
+    if flags and (valid is None or valid.numel() != m):
+        raise ValueError("ln_residual: masking needs a valid-token mask with one entry per row")
+    if valid is not None and valid.dtype not in (torch.bool, torch.uint8):
+        raise ValueError("ln_residual: valid must be bool or uint8")
+    if valid is not None and not valid.is_contiguous():
+        valid = valid.contiguous()
+    if write_x:
+        flags |= _abi.TF_LN_WRITE_X
+        if x_out is None:
+            x_out = torch.empty_like(x)
+    if out_dtype == torch.float32:
+        flags |= _abi.TF_LN_OUT_F32
+    elif out_dtype != torch.float16:
+        raise ValueError("ln_residual: out_dtype must be fp16 or fp32")
+    if normed is None:
+        normed = torch.empty(x.shape, dtype=out_dtype, device=x.device)
+    _abi.call("tf_ln_residual", _ptr(x), _ptr(delta), _ptr(weight), _ptr(bias), float(eps),
+              _ptr(valid) if flags & 7 else None, m, d, flags, _ptr(x_out), _ptr(normed), _stream())
+    return (x_out if write_x else x), normed
+
+
+def linear(a: torch.Tensor, w: torch.Tensor, b: torch.Tensor, *, gelu: bool = False,
+           out: Optional[torch.Tensor] = None, tile_n: int = 0) -> torch.Tensor:
+    """fp16 GEMM on tcgen05 (tf_gemm): out = [gelu](a @ w.T + b), a [..., K]
+    fp16 with unit inner stride, w [N, K] fp16, b [N] fp16."""
+    _need_cuda("linear", a, w, b, out)
+    if a.dtype != torch.float16 or w.dtype != torch.float16 or b.dtype != torch.float16:
+        raise ValueError("linear: a, w and b must be fp16")
+    k = a.shape[-1]
+    n = w.shape[0]
+    a2 = a.reshape(-1, k)
+    if a2.stride(-1) != 1 or w.stride(-1) != 1 or not b.is_contiguous():
+        raise ValueError("linear: operands need a unit inner stride")
+    m = a2.shape[0]
+    if out is None:
+        out = torch.empty(*a.shape[:-1], n, dtype=torch.float16, device=a.device)
+    o2 = out.view(-1, n) if out.is_contiguous() else out
+    if o2.stride(-1) != 1:
+        raise ValueError("linear: out needs a unit inner stride")
+    epi = _abi.TF_EPI_BIAS_GELU if gelu else _abi.TF_EPI_BIAS
+    if tile_n:
+        _abi.call("tf_gemm_tiled", _ptr(a2), a2.stride(0), _ptr(w), w.stride(0), _ptr(b), _ptr(o2), o2.stride(0),
+                  m, n, k, epi, tile_n, _stream())
+    else:
+        _abi.call("tf_gemm", _ptr(a2), a2.stride(0), _ptr(w), w.stride(0), _ptr(b), _ptr(o2), o2.stride(0),
+                  m, n, k, epi, _stream())
+    return out
+
+
+def flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, heads: int, scale: float, *,
+                    causal: bool = False, key_valid: Optional[torch.Tensor] = None, q_pos0: int = 0,
+                    k_pos0: int = 0, out: Optional[torch.Tensor] = None, out_dtype: torch.dtype = torch.float16,
+                    lse: Optional[torch.Tensor] = None, want_lse: bool = False):
+    """Flash attention forward (tf_flash_fwd).
+
+    q: [B, Sq, H*hd] fp16 view with unit inner stride (may be a column slice
+    of a packed QKV buffer), k, v: [B, Sk, H*hd] likewise. Returns out
+    [B, Sq, H*hd] (fp16 or fp32) and, with want_lse or an lse buffer, the
+    natural-log sum-exp [B, H, Sq] fp32."""
+    _need_cuda("flash_attention", q, k, v, key_valid, out, lse)
+    for t in (q, k, v):
+        if t.dtype != torch.float16 or t.dim() != 3 or t.stride(-1) != 1:
+            raise ValueError("flash_attention: q, k, v must be fp16 [B, S, H*hd] with unit inner stride")
+    bsz, sq, dq = q.shape
+    sk = k.shape[1]
+    if k.shape != v.shape or k.shape[0] != bsz or k.shape[2] != dq or v.stride() != k.stride():
+        raise ValueError("flash_attention: k and v must have matching shapes and strides")
+    if dq % heads:
+        raise ValueError("flash_attention: feature width not divisible by heads")
+    hd = dq // heads
+    if out is None:
+        out = torch.empty(bsz, sq, dq, dtype=out_dtype, device=q.device)
+    if out.stride(-1) != 1 or out.dtype != out_dtype:
+        raise ValueError("flash_attention: out must match out_dtype with unit inner stride")
+    if lse is None and want_lse:
+        lse = torch.empty(bsz, heads, sq, dtype=torch.float32, device=q.device)
+    if key_valid is not None:
+        if key_valid.shape != (bsz, sk) or key_valid.dtype not in (torch.bool, torch.uint8):
+            raise ValueError("flash_attention: key_valid must be bool [B, Sk]")
+        key_valid = key_valid.contiguous()
+    flags = (_abi.TF_ATTN_CAUSAL if causal else 0) | (_abi.TF_ATTN_OUT_F32 if out_dtype == torch.float32 else 0)
+    _abi.call("tf_flash_fwd", _ptr(q), _ptr(k), _ptr(v), q.stride(1), k.stride(1), q.stride(0), k.stride(0),
+              _ptr(out), out.stride(1), out.stride(0), _ptr(lse), _ptr(key_valid), bsz, heads, sq, sk, hd,
+              float(scale), int(q_pos0), int(k_pos0), flags, _stream())
+    return out, lse
+
+
+def attn_merge(o_acc: torch.Tensor, lse_acc: torch.Tensor, o_part: torch.Tensor, lse_part: torch.Tensor,
+               heads: int, out16: Optional[torch.Tensor] = None) -> None:
+    """Merge a partial attention result into a running one in place
+    (tf_attn_merge); optionally also write the merged result as fp16."""
+    _need_cuda("attn_merge", o_acc, lse_acc, o_part, lse_part, out16)
+    for t in (o_acc, o_part, lse_acc, lse_part):
+        if t.dtype != torch.float32:
+            raise ValueError("attn_merge: accumulators must be fp32")
+    if o_acc.stride() != o_part.stride() or o_acc.shape != o_part.shape:
+        raise ValueError("attn_merge: o_acc and o_part must share shape and strides")
+    if not (lse_acc.is_contiguous() and lse_part.is_contiguous()):
+        raise ValueError("attn_merge: lse tensors must be contiguous")
+    bsz, sq, dq = o_acc.shape
+    ld16 = out16.stride(1) if out16 is not None else 0
+    bs16 = out16.stride(0) if out16 is not None else 0
+    _abi.call("tf_attn_merge", _ptr(o_acc), _ptr(lse_acc), _ptr(o_part), _ptr(lse_part), o_acc.stride(1),
+              o_acc.stride(0), _ptr(out16), ld16, bs16, bsz, heads, sq, dq // heads, _stream())
