@@ -46,13 +46,22 @@ extern "C" {
 #define TF_LN_WRITE_X 8    /* store the updated residual into x_out */
 #define TF_LN_OUT_F32 16   /* normed is fp32 (default fp16) */
 
-/* tf_gemm epilogues */
-#define TF_EPI_BIAS 0      /* C = fp16(acc + bias) */
-#define TF_EPI_BIAS_GELU 1 /* C = fp16(gelu_erf(fp16(acc + bias))) */
+/* tf_gemm epilogues (low bits) and options */
+#define TF_EPI_BIAS 0       /* C = fp16(acc + bias) */
+#define TF_EPI_BIAS_GELU 1  /* C = fp16(gelu_erf(acc + bias)), GELU in fp32 */
+#define TF_EPI_W_SPLIT 16   /* W is [N, 2K] = [W_hi | W_lo] (W_lo = fp16(W - W_hi)) */
+
+/* tf_gemm_residual mask modes (the reference's two masking points) */
+#define TF_RES_NO_MASK 0
+#define TF_RES_MASK_DELTA 1 /* invalid rows: x_out = x_in (delta zeroed) */
+#define TF_RES_MASK_X 2     /* invalid rows: x_out = 0 */
 
 /* tf_flash_fwd flags */
 #define TF_ATTN_CAUSAL 1  /* mask key position > query position */
 #define TF_ATTN_OUT_F32 2 /* out is fp32 (default fp16) */
+#define TF_ATTN_EXP_F32 4 /* fp32 exp2 for the probabilities (default: the
+                             packed fp16 exp2 unit; P is rounded to fp16 for
+                             the PV product either way) */
 
 /* ABI version, bumped on any signature change. */
 int tf_abi_version(void);
@@ -80,19 +89,30 @@ int tf_ln_residual(const float* x, const void* delta, const float* w, const floa
 
 /* fp16 GEMM, fp32 accumulation on tcgen05 tensor cores:
  *   C[M, N] = epilogue(A[M, K] * W[N, K]^T + bias[N])
- * A row-major with pitch lda, W = nn.Linear weight [N, K] with pitch ldw,
- * C row-major with pitch ldc; all fp16. N % 32 == 0, K and pitches % 8 == 0,
- * pointers 16-byte aligned.
+ * A row-major with pitch lda, W = nn.Linear weight [N, K] (or [N, 2K] with
+ * TF_EPI_W_SPLIT) with pitch ldw, C row-major with pitch ldc; A, W, C fp16,
+ * bias fp32. N % 32 == 0, K and pitches % 8 == 0, pointers 16-byte aligned.
  * Replaces _lin / _triton_linear / _triton_gemm_gelu / F.linear on the
  * fp16-GEMM path (torch_transformer_benchmark.py:4138-4194, 1860-1906,
  * kernel 1756-1803). */
-int tf_gemm(const void* A, int64_t lda, const void* W, int64_t ldw, const void* bias, void* C, int64_t ldc,
+int tf_gemm(const void* A, int64_t lda, const void* W, int64_t ldw, const float* bias, void* C, int64_t ldc,
             int64_t M, int64_t N, int64_t K, int epilogue, void* stream);
 
 /* tf_gemm with an explicit N tile (64, 128 or 256; 0 = automatic). For
  * tuning and tests. */
-int tf_gemm_tiled(const void* A, int64_t lda, const void* W, int64_t ldw, const void* bias, void* C,
+int tf_gemm_tiled(const void* A, int64_t lda, const void* W, int64_t ldw, const float* bias, void* C,
                   int64_t ldc, int64_t M, int64_t N, int64_t K, int epilogue, int tile_n, void* stream);
+
+/* GEMM whose epilogue closes a residual connection in fp32:
+ *   x_out[M, N] = mask_x(x_in + mask_delta(A * W^T + bias))
+ * x_in / x_out fp32 with pitch ldx (x_out may equal x_in: in place); valid
+ * uint8 [M] for the mask modes. w_split != 0: W is [N, 2K] = [W_hi | W_lo].
+ * Replaces out_proj / ffn_out (torch_transformer_benchmark.py:4163-4169,
+ * 4194) together with the residual add of the following _ln_site
+ * (torch_transformer_benchmark.py:3988-3995). */
+int tf_gemm_residual(const void* A, int64_t lda, const void* W, int64_t ldw, const float* bias,
+                     const float* x_in, float* x_out, int64_t ldx, const uint8_t* valid, int mask_mode,
+                     int64_t M, int64_t N, int64_t K, int w_split, void* stream);
 
 /* Flash attention forward (online softmax, no score matrix in HBM):
  *   out[b, i, h*hd:(h+1)*hd] = sum_j softmax_j(scale * q_i . k_j) v_j

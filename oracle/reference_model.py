@@ -304,16 +304,33 @@ def ln_site(x: torch.Tensor, delta: Optional[torch.Tensor], w: torch.Tensor, b: 
     return x, y
 
 
-def linear_fp16(a16: torch.Tensor, w16: torch.Tensor, b16: torch.Tensor,
+def linear_fp16(a16: torch.Tensor, w16: torch.Tensor, b: torch.Tensor,
                 gelu: bool) -> torch.Tensor:
-    """fp16 GEMM with fp32 accumulation, + bias, rounded to fp16, then (for the
-    FFN-in projection) exact-erf GELU on the rounded value and rounded again -
-    the order of _gemm_gelu_kernel (torch_transformer_benchmark.py:1795-1802).
-    Returns the fp16 result as fp32 values."""
-    h = (a16.double() @ w16.double().t() + b16.double()).float().half().float()
+    """fp16 operands, exact (fp64) accumulation, + bias, [exact-erf GELU],
+    rounded once to fp16 - the projection of the reference's fp16-GEMM path
+    (torch_transformer_benchmark.py:4138-4194, kernel 1756-1803) without its
+    intermediate fp16 rounding of the bias and of the GELU input. Returns the
+    fp16 result as fp32 values."""
+    h = a16.double() @ w16.double().t() + b.double()
     if gelu:
-        h = F.gelu(h, approximate="none").half().float()
-    return h
+        h = F.gelu(h, approximate="none")
+    return h.float().half().float()
+
+
+def linear_residual(a16: torch.Tensor, w: torch.Tensor, b: torch.Tensor, x_in: torch.Tensor,
+                    valid: Optional[torch.Tensor], mask_delta: bool, mask_x: bool) -> torch.Tensor:
+    """x_in + mask_delta(a16 @ w^T + b), then mask_x, in fp64 rounded to fp32:
+    the residual add of the reference's LayerNorm sites
+    (torch_transformer_benchmark.py:3988-3995) applied to a projection output
+    kept in full precision. `w` is the weight the product should see (fp16
+    values, or the fp32 weight for split-weight GEMMs)."""
+    delta = a16.double() @ w.double().t() + b.double()
+    if valid is not None and mask_delta:
+        delta = delta.masked_fill(~valid.reshape(-1, 1).bool(), 0)
+    y = x_in.double() + delta
+    if valid is not None and mask_x:
+        y = y.masked_fill(~valid.reshape(-1, 1).bool(), 0)
+    return y.float()
 
 
 def attention_fp16(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float,

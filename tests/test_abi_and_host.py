@@ -1,0 +1,124 @@
+"""CPU-only checks of the boundary and the host logic (no kernel launches).
+
+* the C-ABI library loads and exports every function include/tfb200.h
+  declares, with the argument count the ctypes binding uses;
+* the module tree / state_dict contract with the reference
+  (torch_transformer_benchmark.py:135-248, 4328-4338);
+* TransformerConfig validation (torch_transformer_benchmark.py:52-70) and the
+  reference's FLOP convention (run_bench.py:102-113);
+* the product path refuses CPU tensors instead of falling back.
+"""
+
+import ctypes
+import re
+import subprocess
+from pathlib import Path
+
+import pytest
+import torch
+
+from oracle import reference_model as om
+from transformer_optimization_b200 import (NAMED_CONFIGS, BaselineTransformer, TransformerConfig,
+                                           UserOptimizedTransformer, copy_model_weights, count_causal_flops,
+                                           count_dense_flops)
+from transformer_optimization_b200 import _abi
+
+ROOT = Path(__file__).resolve().parent.parent
+HEADER = ROOT / "include" / "tfb200.h"
+
+
+def _declared():
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    out = {}
+    for m in re.finditer(r"\b(?:int|const char\s*\*)\s*(tf_\w+)\s*\(([^)]*)\)\s*;", text):
+        args = [a for a in m.group(2).split(",") if a.strip() and a.strip() != "void"]
+        out[m.group(1)] = len(args)
+    return out
+
+
+@pytest.fixture(scope="module")
+def lib():
+    if not _abi.LIB_PATH.exists():
+        from transformer_optimization_b200 import build
+        build.build()
+    return _abi.load()
+
+
+def test_header_symbols_exported(lib):
+    declared = _declared()
+    assert set(declared) == set(_abi.SIGNATURES), "ctypes binding and header disagree"
+    nm = subprocess.run(["nm", "-D", "--defined-only", str(_abi.LIB_PATH)], capture_output=True, text=True).stdout
+    exported = set(re.findall(r"\bT (tf_\w+)", nm))
+    for name, nargs in declared.items():
+        assert name in exported, f"{name} not exported"
+        assert isinstance(getattr(lib, name), ctypes._CFuncPtr)
+        assert len(_abi.SIGNATURES[name][0]) == nargs, f"{name}: header has {nargs} args"
+
+
+def test_abi_version_and_error_string(lib):
+    assert lib.tf_abi_version() == 2
+    assert isinstance(lib.tf_last_error(), bytes)
+
+
+def test_missing_library_is_loud(tmp_path):
+    with pytest.raises(RuntimeError, match="missing"):
+        _abi.load(tmp_path / "nope.so")
+
+
+def test_state_dict_contract():
+    cfg = TransformerConfig(2, 16, 64, 4, 128, 3, False)
+    torch.manual_seed(0)
+    opt = UserOptimizedTransformer(cfg)
+    p = om.init_params(cfg, 0)
+    sd = opt.state_dict()
+    assert list(sd) == list(p)
+    assert all(torch.equal(sd[k], p[k]) for k in p)  # same init draws under the same seed
+    opt.load_state_dict(p, strict=True)
+    base = BaselineTransformer(cfg)
+    copy_model_weights(opt, base, strict=True)
+    # no parameters or buffers beyond the reference's
+    assert len(list(opt.buffers())) == 0
+    assert sum(1 for _ in opt.parameters()) == sum(1 for _ in base.parameters())
+
+
+def test_product_refuses_cpu():
+    cfg = NAMED_CONFIGS["c1"]
+    m = UserOptimizedTransformer(cfg)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        m(torch.randn(2, 128, 256))
+    with pytest.raises(NotImplementedError):
+        BaselineTransformer(cfg)(torch.randn(2, 128, 256))
+
+
+def test_config_validation():
+    with pytest.raises(ValueError, match="divisible"):
+        TransformerConfig(1, 8, 30, 4, 8, 1, False).validate()
+    for bad in ((0, 8, 32, 4, 8, 1), (1, 0, 32, 4, 8, 1), (1, 8, 32, 4, 0, 1), (1, 8, 32, 4, 8, 0)):
+        with pytest.raises(ValueError):
+            TransformerConfig(*bad, False).validate()
+
+
+def test_flop_convention():
+    # run_bench.py:102-113 numbers for the BASELINE configs
+    assert count_dense_flops(NAMED_CONFIGS["c1"]) == 872415232
+    assert abs(count_dense_flops(NAMED_CONFIGS["c3"]) / 1e12 - 6.597) < 1e-3
+    assert abs(count_dense_flops(NAMED_CONFIGS["c4"]) / 1e12 - 422.2) < 0.1
+    assert abs(count_dense_flops(NAMED_CONFIGS["c5"]) / 1e12 - 173.9) < 0.1
+    c = TransformerConfig(1, 100, 64, 2, 64, 1, True)
+    assert count_causal_flops(c) < count_dense_flops(c)
+
+
+def test_mask_resolution_memoised(monkeypatch):
+    m = UserOptimizedTransformer(NAMED_CONFIGS["c1"])
+    mask = torch.ones(2, 128, dtype=torch.bool)
+    calls = []
+    real_all = torch.all
+    monkeypatch.setattr(torch, "all", lambda t: calls.append(1) or real_all(t))
+    assert m._resolve_mask_active(mask) is False
+    assert m._resolve_mask_active(mask) is False
+    assert len(calls) == 1
+    mask2 = mask.clone()
+    mask2[1, 100:] = False
+    assert m._resolve_mask_active(mask2) is True
+    assert m._resolve_mask_active(None) is False

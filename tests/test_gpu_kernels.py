@@ -81,16 +81,22 @@ GEMM_SHAPES = [  # (M, K, N): model projections at small M plus ragged rows
 ]
 
 
+def _gemm_inputs(m, k, n, seed):
+    g = torch.Generator().manual_seed(seed)
+    a = torch.randn(m, k, generator=g).half()
+    bound = 1 / math.sqrt(k)
+    w = (torch.rand(n, k, generator=g) * 2 - 1).mul(bound)
+    bias = (torch.rand(n, generator=g) * 2 - 1).mul(bound)
+    return a, w, bias
+
+
 @pytest.mark.parametrize("m,k,n", GEMM_SHAPES)
 @pytest.mark.parametrize("gelu", [False, True])
 def test_gemm(K, m, k, n, gelu):
-    g = torch.Generator().manual_seed(m + 7 * k + 13 * n)
-    a = torch.randn(m, k, generator=g).half()
-    bound = 1 / math.sqrt(k)
-    w = (torch.rand(n, k, generator=g) * 2 - 1).mul(bound).half()
-    bias = (torch.rand(n, generator=g) * 2 - 1).mul(bound).half()
-    ref = om.linear_fp16(a, w, bias, gelu)
-    out = K.linear(a.cuda(), w.cuda(), bias.cuda(), gelu=gelu).float().cpu()
+    a, w, bias = _gemm_inputs(m, k, n, m + 7 * k + 13 * n)
+    w16 = w.half()
+    ref = om.linear_fp16(a, w16, bias, gelu)
+    out = K.linear(a.cuda(), w16.cuda(), bias.cuda(), gelu=gelu).float().cpu()
     err = (out - ref).abs()
     assert torch.all(err <= 2e-3 * ref.abs() + 1e-3), f"max err {err.max()}"
 
@@ -98,26 +104,68 @@ def test_gemm(K, m, k, n, gelu):
 @pytest.mark.parametrize("tile_n", [64, 128, 256])
 def test_gemm_tiles(K, tile_n):
     m, k, n = 777, 1024, 1536
-    g = torch.Generator().manual_seed(tile_n)
-    a = torch.randn(m, k, generator=g).half()
-    w = (torch.randn(n, k, generator=g) / 32).half()
-    bias = torch.randn(n, generator=g).half()
-    ref = om.linear_fp16(a, w, bias, False)
-    out = K.linear(a.cuda(), w.cuda(), bias.cuda(), tile_n=tile_n).float().cpu()
+    a, w, bias = _gemm_inputs(m, k, n, tile_n)
+    w16 = w.half()
+    ref = om.linear_fp16(a, w16, bias, False)
+    out = K.linear(a.cuda(), w16.cuda(), bias.cuda(), tile_n=tile_n).float().cpu()
     assert torch.all((out - ref).abs() <= 2e-3 * ref.abs() + 1e-3)
 
 
 def test_gemm_strided_output(K):
     """QKV-style: write into a column slice of a wider buffer."""
     m, k, n = 200, 512, 512
-    a = torch.randn(m, k).half().cuda()
-    w = (torch.randn(n, k) / 23).half().cuda()
-    bias = torch.zeros(n).half().cuda()
+    a, w, bias = _gemm_inputs(m, k, n, 9)
+    w16 = w.half()
     big = torch.zeros(m, 3 * n, dtype=torch.float16, device="cuda")
-    K.linear(a, w, bias, out=big[:, n:2 * n])
-    ref = om.linear_fp16(a.cpu(), w.cpu(), bias.cpu(), False)
+    K.linear(a.cuda(), w16.cuda(), bias.cuda(), out=big[:, n:2 * n])
+    ref = om.linear_fp16(a, w16, bias, False)
     assert torch.all(((big[:, n:2 * n].float().cpu()) - ref).abs() <= 2e-3 * ref.abs() + 1e-3)
     assert torch.count_nonzero(big[:, :n]) == 0 and torch.count_nonzero(big[:, 2 * n:]) == 0
+
+
+@pytest.mark.parametrize("m,k,n", [(300, 1024, 1024), (64, 2048, 512), (1000, 4096, 2048), (129, 200, 256)])
+@pytest.mark.parametrize("mode", ["none", "mask_delta", "mask_x"])
+def test_gemm_residual(K, m, k, n, mode):
+    """fp32 residual epilogue: x_out = mask_x(x_in + mask_delta(a @ w.T + b)).
+    The delta is an fp32-accumulated sum of fp16 products: |d| <= 1e-4 + 1e-5|x|."""
+    a, w, bias = _gemm_inputs(m, k, n, m + k + n)
+    w16 = w.half()
+    g = torch.Generator().manual_seed(1)
+    x = torch.randn(m, n, generator=g) * 3
+    valid = torch.rand(m, generator=g) > 0.25
+    md, mx = mode == "mask_delta", mode == "mask_x"
+    ref = om.linear_residual(a, w16, bias, x, valid, md, mx)
+    xg = x.cuda()
+    out = K.linear_residual(a.cuda(), w16.cuda(), bias.cuda(), xg, None, valid.cuda(), mask_delta=md, mask_x=mx)
+    assert torch.equal(xg.cpu(), x)  # x_in untouched when x_out is separate
+    assert torch.allclose(out.cpu(), ref, atol=1e-4, rtol=1e-5)
+    # in place
+    K.linear_residual(a.cuda(), w16.cuda(), bias.cuda(), xg, xg, valid.cuda(), mask_delta=md, mask_x=mx)
+    assert torch.allclose(xg.cpu(), ref, atol=1e-4, rtol=1e-5)
+    if mx:
+        assert torch.count_nonzero(xg.cpu()[~valid]) == 0
+    if md:
+        assert torch.equal(xg.cpu()[~valid], x[~valid])
+
+
+@pytest.mark.parametrize("k", [1024, 8192, 200])
+def test_gemm_split_weight(K, k):
+    """[W_hi | W_lo] weights reproduce the fp32 weight: the error against the
+    fp32-weight product is far below the plain fp16-weight error."""
+    m, n = 256, 512
+    a, w, bias = _gemm_inputs(m, k, n, k)
+    x = torch.zeros(m, n)
+    ref = om.linear_residual(a, w, bias, x, None, False, False)  # fp32 weight
+    plain = K.linear_residual(a.cuda(), w.half().cuda(), bias.cuda(), x.cuda()).cpu()
+    split = K.linear_residual(a.cuda(), K.split_weight(w).cuda(), bias.cuda(), x.cuda(), w_split=True).cpu()
+    e_plain = (plain - ref).abs().max().item()
+    e_split = (split - ref).abs().max().item()
+    assert e_split < e_plain / 8, (e_split, e_plain)
+    assert torch.allclose(split, ref, atol=1e-4, rtol=1e-5)
+    # the fp16-output GEMM takes split weights too
+    out16 = K.linear(a.cuda(), K.split_weight(w).cuda(), bias.cuda(), w_split=True).float().cpu()
+    r16 = ref.half().float()
+    assert torch.all((out16 - r16).abs() <= 2e-3 * r16.abs() + 1e-3)
 
 
 # ----------------------------------------------------------------- attention
@@ -141,7 +189,8 @@ def _qkv(b, h, s, hd, seed):
 
 
 @pytest.mark.parametrize("b,h,sq,sk,hd,causal,masked", ATTN_CASES)
-def test_flash_packed_qkv(K, b, h, sq, sk, hd, causal, masked):
+@pytest.mark.parametrize("exp_f32", [False, True])
+def test_flash_packed_qkv(K, b, h, sq, sk, hd, causal, masked, exp_f32):
     d = h * hd
     qkv = _qkv(b, h, sq, hd, sq + hd)
     kv_valid = None
@@ -154,7 +203,8 @@ def test_flash_packed_qkv(K, b, h, sq, sk, hd, causal, masked):
     ref = ref.transpose(1, 2).reshape(b, sq, d)
     g = qkv.cuda()
     out, lse = K.flash_attention(g[..., :d], g[..., d:2 * d], g[..., 2 * d:], h, hd ** -0.5, causal=causal,
-                                 key_valid=None if kv_valid is None else kv_valid.cuda(), want_lse=True)
+                                 key_valid=None if kv_valid is None else kv_valid.cuda(), want_lse=True,
+                                 exp_f32=exp_f32)
     out = out.float().cpu()
     err = (out - ref).abs()
     assert torch.all(err <= 1e-2 * ref.abs() + 3e-3), f"max err {err.max()}"

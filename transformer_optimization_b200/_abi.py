@@ -33,9 +33,15 @@ TF_LN_OUT_F32 = 16
 
 TF_EPI_BIAS = 0
 TF_EPI_BIAS_GELU = 1
+TF_EPI_W_SPLIT = 16
+
+TF_RES_NO_MASK = 0
+TF_RES_MASK_DELTA = 1
+TF_RES_MASK_X = 2
 
 TF_ATTN_CAUSAL = 1
 TF_ATTN_OUT_F32 = 2
+TF_ATTN_EXP_F32 = 4
 
 # every symbol include/tfb200.h declares, with its ctypes signature
 _P = ctypes.c_void_p
@@ -49,6 +55,7 @@ SIGNATURES = {
     "tf_ln_residual": ([_P, _P, _P, _P, _F, _P, _I64, _I64, _I, _P, _P, _P], _I),
     "tf_gemm": ([_P, _I64, _P, _I64, _P, _P, _I64, _I64, _I64, _I64, _I, _P], _I),
     "tf_gemm_tiled": ([_P, _I64, _P, _I64, _P, _P, _I64, _I64, _I64, _I64, _I, _I, _P], _I),
+    "tf_gemm_residual": ([_P, _I64, _P, _I64, _P, _P, _P, _I64, _P, _I, _I64, _I64, _I64, _I, _P], _I),
     "tf_flash_fwd": ([_P, _P, _P, _I64, _I64, _I64, _I64, _P, _I64, _I64, _P, _P,
                       _I64, _I64, _I64, _I64, _I64, _F, _I64, _I64, _I, _P], _I),
     "tf_attn_merge": ([_P, _P, _P, _P, _I64, _I64, _P, _I64, _I64, _I64, _I64, _I64, _I64, _P], _I),

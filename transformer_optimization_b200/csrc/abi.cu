@@ -156,7 +156,7 @@ static inline int begin_call() {
 
 extern "C" {
 
-int tf_abi_version(void) { return 1; }
+int tf_abi_version(void) { return 2; }
 
 const char* tf_last_error(void) { return tfb::g_msg; }
 
@@ -186,21 +186,66 @@ int tf_ln_residual(const float* x, const void* delta, const float* w, const floa
                           as_stream(stream));
 }
 
-int tf_gemm(const void* A, int64_t lda, const void* W, int64_t ldw, const void* bias, void* C, int64_t ldc,
+static int gemm_common(const void* A, int64_t lda, const void* W, int64_t ldw, const float* bias, void* C,
+                       int64_t ldc, int64_t M, int64_t N, int64_t K, int epilogue, int tile_n, void* stream) {
+  if (epilogue & ~(0xF | TF_EPI_W_SPLIT)) return set_error(TF_ERR_SHAPE, "tf_gemm: unknown epilogue bits");
+  tfb::GemmCall g = {};
+  g.A = A;
+  g.lda = lda;
+  g.W = W;
+  g.ldw = ldw;
+  g.bias = bias;
+  g.C = C;
+  g.ldc = ldc;
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.epilogue = epilogue & 0xF;
+  if (g.epilogue > 1) return set_error(TF_ERR_SHAPE, "tf_gemm: epilogue %d", g.epilogue);
+  g.a_repeat = (epilogue & TF_EPI_W_SPLIT) ? 2 : 1;
+  g.tile_n = tile_n;
+  return tfb::gemm_f16(g, as_stream(stream));
+}
+
+int tf_gemm(const void* A, int64_t lda, const void* W, int64_t ldw, const float* bias, void* C, int64_t ldc,
             int64_t M, int64_t N, int64_t K, int epilogue, void* stream) {
   int rc = begin_call();
   if (rc) return rc;
-  return tfb::gemm_f16(A, lda, W, ldw, bias, C, ldc, M, N, K, epilogue, 0, as_stream(stream));
+  return gemm_common(A, lda, W, ldw, bias, C, ldc, M, N, K, epilogue, 0, stream);
 }
 
-int tf_gemm_tiled(const void* A, int64_t lda, const void* W, int64_t ldw, const void* bias, void* C,
+int tf_gemm_tiled(const void* A, int64_t lda, const void* W, int64_t ldw, const float* bias, void* C,
                   int64_t ldc, int64_t M, int64_t N, int64_t K, int epilogue, int tile_n, void* stream) {
   int rc = begin_call();
   if (rc) return rc;
   if (tile_n != 0 && tile_n != 64 && tile_n != 128 && tile_n != 256)
     return set_error(TF_ERR_SHAPE, "tf_gemm_tiled: tile_n=%d (0, 64, 128 or 256)", tile_n);
   if (tile_n != 0 && N % tile_n != 0) return set_error(TF_ERR_SHAPE, "tf_gemm_tiled: N %% tile_n != 0");
-  return tfb::gemm_f16(A, lda, W, ldw, bias, C, ldc, M, N, K, epilogue, tile_n, as_stream(stream));
+  return gemm_common(A, lda, W, ldw, bias, C, ldc, M, N, K, epilogue, tile_n, stream);
+}
+
+int tf_gemm_residual(const void* A, int64_t lda, const void* W, int64_t ldw, const float* bias,
+                     const float* x_in, float* x_out, int64_t ldx, const uint8_t* valid, int mask_mode,
+                     int64_t M, int64_t N, int64_t K, int w_split, void* stream) {
+  int rc = begin_call();
+  if (rc) return rc;
+  tfb::GemmCall g = {};
+  g.A = A;
+  g.lda = lda;
+  g.W = W;
+  g.ldw = ldw;
+  g.bias = bias;
+  g.x_in = x_in;
+  g.x_out = x_out;
+  g.ldx = ldx;
+  g.valid = valid;
+  g.mask_mode = mask_mode;
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.epilogue = 2;
+  g.a_repeat = w_split ? 2 : 1;
+  return tfb::gemm_f16(g, as_stream(stream));
 }
 
 int tf_flash_fwd(const void* q, const void* k, const void* v, int64_t ld_q, int64_t ld_kv, int64_t bs_q,

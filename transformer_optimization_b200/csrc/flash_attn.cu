@@ -6,21 +6,29 @@
 // (F.scaled_dot_product_attention / _short_attn_kernel / _flash_attn_kernel,
 // torch_transformer_benchmark.py:4146-4161, 1193-1418). Like the reference's
 // flash kernel it never materialises the score matrix: scores live in TMEM,
-// probabilities in shared memory, one 128-key block at a time, with the
-// online-softmax running max / sum (m, l) per query row and exp2 with the
-// scale folded into log2(e) (torch_transformer_benchmark.py:1427-1428).
+// probabilities in shared memory, one 128-key block at a time, with a running
+// max per query row and exp2 with the scale folded into log2(e)
+// (torch_transformer_benchmark.py:1427-1428).
 //
-// One CTA = one 128-query tile of one (batch, head); 192 threads:
-//   warp 0      TMA producer: the Q tile once, then K_j / V_j blocks
-//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer:
-//                 S_j = Q K_j^T          -> TMEM S[j%2]   (fp32, 128 cols)
-//                 O_j = P_j V_j          -> TMEM O[j%2]   (fp32, hd cols)
-//   warps 2..5  softmax + correction: thread t owns query row t. It reads
-//               S_j from TMEM, writes P_j (fp16, 128B-swizzled K-major) to
-//               shared memory, and folds O_j into its fp32 register
-//               accumulator with the running-max rescale.
-// S_{j+1} is issued while the softmax warps work on S_j (two S buffers), so
-// the tensor core and the softmax overlap.
+// One CTA = two 128-query tiles of one (batch, head), 384 threads:
+//   warp 0        TMA producer: both Q tiles, then the K_j blocks
+//   warp 1        TMEM allocator + single-thread tcgen05.mma issuer
+//   warp 2        TMA producer of the V_j blocks
+//   warps 4..7    softmax of tile 0 (thread = query row)
+//   warps 8..11   softmax of tile 1
+// Per key block j and tile t the MMA thread issues
+//   S_t = Q_t K_j^T   -> TMEM (fp32, 128 columns)
+//   O_t += P_t V_j    -> TMEM (fp32, accumulated over all blocks)
+// and the two softmax warpgroups alternate, so one tile's exponentials run
+// while the tensor core works on the other tile.
+//
+// Online softmax with lazy rescaling: a row keeps a reference max m; P =
+// exp2(s*c - m) is computed against it, and O (and l) are rescaled in TMEM
+// only when the row max grows by more than 8 (log2 units), so P <= 2^8 stays
+// well inside fp16. The final O/l is the exact softmax either way.
+// For head_dim 64 the row sum l comes out of the tensor core: V is extended
+// by a constant column block whose first column is 1.0, so O column 64 holds
+// sum_j P_j, computed from exactly the fp16 P that multiplies V.
 //
 // The kernel also emits the natural-log sum-exp per row, used to merge the
 // partial results of context-parallel ring attention exactly.
@@ -29,9 +37,18 @@
 
 namespace tfb {
 
-constexpr int kAttnBM = 128;  // query rows per CTA
+constexpr int kAttnBM = 128;  // query rows per tile
 constexpr int kAttnBN = 128;  // keys per block
-constexpr int kAttnThreads = 192;
+constexpr int kAttnTiles = 2;
+constexpr int kAttnThreads = 384;
+constexpr float kRescaleThreshold = 8.0f;
+// Register split: the kernel is built at 168 registers/thread (384 threads,
+// 64512 per CTA); warpgroup 0 (producers, MMA) drops to 40 and the two
+// softmax warpgroups rise to 232: 128*40 + 256*232 = 64512, the launch pool.
+constexpr int kRegsLaunch = 168;
+constexpr int kRegsLow = 40;
+constexpr int kRegsHigh = 232;
+static_assert(128 * kRegsLow + 256 * kRegsHigh <= kAttnThreads * kRegsLaunch, "register split exceeds the pool");
 
 struct AttnKParams {
   void* out;
@@ -39,7 +56,7 @@ struct AttnKParams {
   float* lse;
   const uint8_t* key_valid;
   int heads, seq_q, seq_k;
-  int q_tiles;
+  int q_blocks;      // CTAs along the query axis (256 rows each)
   float scale_log2;  // scale * log2(e)
   long long q_pos0, k_pos0;
   int flags;
@@ -47,82 +64,177 @@ struct AttnKParams {
 };
 
 template <int HD>
-struct AttnSmem {
-  static constexpr int kQBytes = kAttnBM * HD * 2;
-  static constexpr int kKBytes = kAttnBN * HD * 2;
-  static constexpr int kStages = HD == 64 ? 3 : 2;
-  static constexpr int kStageBytes = 2 * kKBytes;  // K then V
-  static constexpr int kPBytes = kAttnBM * kAttnBN * 2;
+struct AttnCfg {
+  static constexpr bool kLFromMma = HD == 64;  // row sum from a ones column of V
+  static constexpr int kNO = kLFromMma ? HD + 16 : HD;  // O columns per tile
+  static constexpr int kKStages = HD == 64 ? 3 : 2;
+  static constexpr int kVStages = HD == 64 ? 3 : 1;
+  static constexpr int kTileBytes = 128 * HD * 2;  // a 128-row x HD fp16 tile
   static constexpr int kQOff = 0;
-  static constexpr int kKVOff = kQOff + kQBytes;
-  static constexpr int kPOff = kKVOff + kStages * kStageBytes;
-  static constexpr int kBarOff = kPOff + 2 * kPBytes;
-  // q_full, kv_full[S], kv_empty[S], s_full[2], s_free[2], p_full[2],
-  // p_free[2], o_full[2], o_free[2], drain, + tmem slot
-  static constexpr int kNumBars = 1 + 2 * kStages + 12 + 1;
+  static constexpr int kKOff = kQOff + kAttnTiles * kTileBytes;
+  static constexpr int kVOff = kKOff + kKStages * kTileBytes;
+  static constexpr int kOnesOff = kVOff + kVStages * kTileBytes;
+  static constexpr int kPOff = kOnesOff + (kLFromMma ? 16384 : 0);
+  static constexpr int kPBytes = kAttnBM * kAttnBN * 2;
+  static constexpr int kBarOff = kPOff + kAttnTiles * kPBytes;
+  // q_full, k_full/empty[KS], v_full/empty[VS], s_full[2], s_free[2],
+  // p_full[2], o_full[2], drain
+  static constexpr int kNumBars = 1 + 2 * kKStages + 2 * kVStages + 8 + 1;
   static constexpr int kBytes = kBarOff + kNumBars * 8 + 16;
   static constexpr int kAlloc = kBytes + 1024;
+  // TMEM columns
+  static constexpr uint32_t kTmS = 0;    // S_t at t*128
+  static constexpr uint32_t kTmO = 256;  // O_t at 256 + t*128
 };
 
-__device__ __forceinline__ float fmax3(float a, float b) { return fmaxf(a, b); }
+__device__ __forceinline__ float ex2_f32(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
-template <int HD>
+// 2^a, 2^b for a pair, through the packed half-precision unit: returns the
+// fp16 pair {2^a (low), 2^b (high)}.
+__device__ __forceinline__ uint32_t ex2_pair_f16(float a, float b) {
+  uint32_t h, r;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(b), "f"(a));
+  asm("ex2.approx.f16x2 %0, %1;" : "=r"(r) : "r"(h));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t pack_f16x2_rn(float a, float b) {
+  uint32_t h;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(b), "f"(a));
+  return h;
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]),
+      "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]),
+      "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// Scale columns [0, NO) of this thread's O row in TMEM by alpha.
+template <int NO>
+__device__ __forceinline__ void rescale_o(uint32_t taddr, float alpha) {
+#pragma unroll
+  for (int c = 0; c < NO / 32; ++c) {
+    uint32_t v[32];
+    tmem_ld32(taddr + c * 32, v);
+    tmem_wait_ld();
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
+    tmem_st32(taddr + c * 32, v);
+  }
+  if constexpr (NO % 32 == 16) {
+    uint32_t v[16];
+    tmem_ld16(taddr + (NO / 32) * 32, v);
+    tmem_wait_ld();
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
+    tmem_st16(taddr + (NO / 32) * 32, v);
+  }
+  tmem_wait_st();
+}
+
+template <int HD, bool EXP16>
 __global__ void __launch_bounds__(kAttnThreads, 1)
     flash_fwd_tcgen05(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                       const __grid_constant__ CUtensorMap tmV, AttnKParams p) {
-  using L = AttnSmem<HD>;
-  constexpr int ST = L::kStages;
+  using C = AttnCfg<HD>;
+  constexpr int KS = C::kKStages;
+  constexpr int VS = C::kVStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
   uint64_t* q_full = bars;
-  uint64_t* kv_full = q_full + 1;
-  uint64_t* kv_empty = kv_full + ST;
-  uint64_t* s_full = kv_empty + ST;
+  uint64_t* k_full = q_full + 1;
+  uint64_t* k_empty = k_full + KS;
+  uint64_t* v_full = k_empty + KS;
+  uint64_t* v_empty = v_full + VS;
+  uint64_t* s_full = v_empty + VS;
   uint64_t* s_free = s_full + 2;
   uint64_t* p_full = s_free + 2;
-  uint64_t* p_free = p_full + 2;
-  uint64_t* o_full = p_free + 2;
-  uint64_t* o_free = o_full + 2;
-  uint64_t* drain = o_free + 2;
+  uint64_t* o_full = p_full + 2;
+  uint64_t* drain = o_full + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
 
   const int warp = warp_id();
   const int lane = lane_id();
-  // longest (causal) tiles first
-  const int q_tile = p.q_tiles - 1 - static_cast<int>(blockIdx.x);
+  const int qb = p.q_blocks - 1 - static_cast<int>(blockIdx.x);  // longest (causal) first
   const int h = blockIdx.y;
   const int b = blockIdx.z;
-  const int q0 = q_tile * kAttnBM;
+  const int q0 = qb * (kAttnBM * kAttnTiles);
+  const bool causal = (p.flags & TF_ATTN_CAUSAL) != 0;
 
-  // number of key blocks this tile needs
-  long long k_end = p.seq_k;
-  if (p.flags & TF_ATTN_CAUSAL) {
-    const long long last_q = p.q_pos0 + q0 + kAttnBM - 1;  // global position of the tile's last row
-    const long long lim = last_q - p.k_pos0 + 1;           // keys [0, lim) can be admissible
-    if (lim < k_end) k_end = lim;
+  // key blocks needed by each tile
+  int nblk[kAttnTiles];
+#pragma unroll
+  for (int t = 0; t < kAttnTiles; ++t) {
+    const int tq0 = q0 + t * kAttnBM;
+    long long k_end = tq0 < p.seq_q ? p.seq_k : 0;
+    if (causal && k_end > 0) {
+      const long long last_q = p.q_pos0 + tq0 + kAttnBM - 1;
+      const long long lim = last_q - p.k_pos0 + 1;
+      if (lim < k_end) k_end = lim;
+    }
+    nblk[t] = k_end <= 0 ? 0 : static_cast<int>((k_end + kAttnBN - 1) / kAttnBN);
   }
-  const int n_blocks = k_end <= 0 ? 0 : static_cast<int>((k_end + kAttnBN - 1) / kAttnBN);
+  const int nmax = nblk[0] > nblk[1] ? nblk[0] : nblk[1];
 
   if (warp == 0 && lane == 0) {
     tma_prefetch_map(&tmQ);
     tma_prefetch_map(&tmK);
     tma_prefetch_map(&tmV);
     mbar_init(q_full, 1);
-    for (int s = 0; s < ST; ++s) {
-      mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+    for (int s = 0; s < KS; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+    }
+    for (int s = 0; s < VS; ++s) {
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&s_free[i], 128);
       mbar_init(&p_full[i], 128);
-      mbar_init(&p_free[i], 1);
       mbar_init(&o_full[i], 1);
-      mbar_init(&o_free[i], 128);
     }
     mbar_init(drain, 1);
     fence_mbar_init();
+  }
+  if constexpr (C::kLFromMma) {
+    // constant "ones" column block: MN-major 128B-swizzled rows of 64 values,
+    // value index 0 (the first head_dim column past V) = 1.0, the rest 0
+    if (warp >= 4) {
+      const int r = threadIdx.x - 128;  // 0..255 -> rows 0..127 (two threads per row)
+      if (r < 256) {
+        const int row = r >> 1;
+        uint4* dst = reinterpret_cast<uint4*>(smem + C::kOnesOff + row * 128);
+#pragma unroll
+        for (int c = (r & 1) * 4; c < (r & 1) * 4 + 4; ++c)
+          dst[c] = make_uint4(c == (row & 7) ? 0x3C00u : 0u, 0u, 0u, 0u);
+      }
+      fence_proxy_async_smem();
+    }
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, 512);
@@ -132,241 +244,307 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  // TMEM columns: S[0] 0..127, S[1] 128..255, O[0] 256.., O[1] 256+HD..
-  const uint32_t tm_s0 = tmem_base;
-  const uint32_t tm_o0 = tmem_base + 256;
-
+  if (warp < 4) {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsLow));
   if (warp == 0) {
-    if (lane == 0 && n_blocks > 0) {
-      // ---------------- TMA producer ----------------
-      mbar_arrive_expect_tx(q_full, L::kQBytes);
+    if (lane == 0 && nmax > 0) {
+      // ---------------- Q + K producer ----------------
+      mbar_arrive_expect_tx(q_full, kAttnTiles * C::kTileBytes);
 #pragma unroll
-      for (int c = 0; c < HD / 64; ++c)
-        tma_load_3d(smem + L::kQOff + c * (kAttnBM * 128), &tmQ, q_full, h * HD + c * 64, q0, b);
+      for (int t = 0; t < kAttnTiles; ++t)
+#pragma unroll
+        for (int c = 0; c < HD / 64; ++c)
+          tma_load_3d(smem + C::kQOff + t * C::kTileBytes + c * 16384, &tmQ, q_full, h * HD + c * 64,
+                      q0 + t * kAttnBM, b);
       int j = 0;
-      for (; j < n_blocks; ++j) {
-        const int s = j % ST;
-        const uint32_t ph = (j / ST) & 1;
-        if (!mbar_wait(&kv_empty[s], ph ^ 1, p.status, kDevTimeoutProducer)) break;
-        uint8_t* kdst = smem + L::kKVOff + s * L::kStageBytes;
-        uint8_t* vdst = kdst + L::kKBytes;
-        mbar_arrive_expect_tx(&kv_full[s], L::kStageBytes);
+      for (; j < nmax; ++j) {
+        const int s = j % KS;
+        if (!mbar_wait(&k_empty[s], ((j / KS) & 1) ^ 1, p.status, kDevTimeoutProducer)) break;
+        mbar_arrive_expect_tx(&k_full[s], C::kTileBytes);
 #pragma unroll
-        for (int c = 0; c < HD / 64; ++c) {
-          tma_load_3d(kdst + c * (kAttnBN * 128), &tmK, &kv_full[s], h * HD + c * 64, j * kAttnBN, b);
-          tma_load_3d(vdst + c * (kAttnBN * 128), &tmV, &kv_full[s], h * HD + c * 64, j * kAttnBN, b);
-        }
+        for (int c = 0; c < HD / 64; ++c)
+          tma_load_3d(smem + C::kKOff + s * C::kTileBytes + c * 16384, &tmK, &k_full[s], h * HD + c * 64,
+                      j * kAttnBN, b);
       }
-      // drain the loads issued above
       mbar_wait(q_full, 0, p.status, kDevTimeoutDrain);
-      const int first = j > ST ? j - ST : 0;
-      for (int i = first; i < j; ++i) mbar_wait(&kv_full[i % ST], (i / ST) & 1, p.status, kDevTimeoutDrain);
+      for (int i = (j > KS ? j - KS : 0); i < j; ++i)
+        mbar_wait(&k_full[i % KS], (i / KS) & 1, p.status, kDevTimeoutDrain);
+    }
+  } else if (warp == 2) {
+    if (lane == 0 && nmax > 0) {
+      // ---------------- V producer ----------------
+      int j = 0;
+      for (; j < nmax; ++j) {
+        const int s = j % VS;
+        if (!mbar_wait(&v_empty[s], ((j / VS) & 1) ^ 1, p.status, kDevTimeoutProducer)) break;
+        mbar_arrive_expect_tx(&v_full[s], C::kTileBytes);
+#pragma unroll
+        for (int c = 0; c < HD / 64; ++c)
+          tma_load_3d(smem + C::kVOff + s * C::kTileBytes + c * 16384, &tmV, &v_full[s], h * HD + c * 64,
+                      j * kAttnBN, b);
+      }
+      for (int i = (j > VS ? j - VS : 0); i < j; ++i)
+        mbar_wait(&v_full[i % VS], (i / VS) & 1, p.status, kDevTimeoutDrain);
     }
   } else if (warp == 1) {
-    if (lane == 0 && n_blocks > 0) {
+    if (lane == 0 && nmax > 0) {
       // ---------------- MMA issuer ----------------
-      constexpr uint32_t idesc_s = idesc_f16_f32(kAttnBM, kAttnBN);             // K-major Q, K-major K
-      constexpr uint32_t idesc_o = idesc_f16_f32(kAttnBM, HD, false, true);     // K-major P, MN-major V
-      const uint32_t sq = smem_u32(smem + L::kQOff);
-      const uint32_t skv = smem_u32(smem + L::kKVOff);
-      const uint32_t sp = smem_u32(smem + L::kPOff);
-      bool ok = mbar_wait(q_full, 0, p.status, kDevTimeoutMma);
-      auto issue_s = [&](int j) -> bool {
-        const int s = j % ST;
-        if (!mbar_wait(&kv_full[s], (j / ST) & 1, p.status, kDevTimeoutMma)) return false;
-        if (!mbar_wait(&s_free[j & 1], ((j >> 1) & 1) ^ 1, p.status, kDevTimeoutMma)) return false;
-        tc_fence_after();
-        const uint32_t kb = skv + s * L::kStageBytes;
+      constexpr uint32_t idesc_s = idesc_f16_f32(kAttnBM, kAttnBN);           // K-major Q, K-major K
+      constexpr uint32_t idesc_o = idesc_f16_f32(kAttnBM, C::kNO, false, true);  // K-major P, MN-major V
+      const uint32_t sbase = smem_u32(smem);
+      auto issue_s = [&](int t, int j) {
+        const uint32_t qa = sbase + C::kQOff + t * C::kTileBytes;
+        const uint32_t ka = sbase + C::kKOff + (j % KS) * C::kTileBytes;
 #pragma unroll
         for (int k = 0; k < HD / 16; ++k) {
-          const uint32_t off = (k >> 2) * (kAttnBM * 128) + (k & 3) * 32;
-          const uint64_t ad = smem_desc_sw128(sq + off, 16, 1024);
-          const uint64_t bd = smem_desc_sw128(kb + (k >> 2) * (kAttnBN * 128) + (k & 3) * 32, 16, 1024);
-          umma_f16_ss(tm_s0 + (j & 1) * 128, ad, bd, idesc_s, k > 0 ? 1u : 0u);
+          const uint32_t off = (k >> 2) * 16384 + (k & 3) * 32;
+          umma_f16_ss(tmem_base + C::kTmS + t * 128, smem_desc_sw128(qa + off, 16, 1024),
+                      smem_desc_sw128(ka + off, 16, 1024), idesc_s, k > 0 ? 1u : 0u);
         }
-        umma_commit(&s_full[j & 1]);
-        return true;
+        umma_commit(&s_full[t]);
       };
-      if (ok) ok = issue_s(0);
-      for (int j = 0; j < n_blocks && ok; ++j) {
-        if (j + 1 < n_blocks) {
-          if (!(ok = issue_s(j + 1))) break;
-        }
-        if (!mbar_wait(&p_full[j & 1], (j >> 1) & 1, p.status, kDevTimeoutMma)) break;
-        if (!mbar_wait(&o_free[j & 1], ((j >> 1) & 1) ^ 1, p.status, kDevTimeoutMma)) break;
-        tc_fence_after();
-        const int s = j % ST;
-        const uint32_t vb = skv + s * L::kStageBytes + L::kKBytes;
-        const uint32_t pb = sp + (j & 1) * L::kPBytes;
+      auto issue_pv = [&](int t, int j) {
+        const uint32_t pa = sbase + C::kPOff + t * C::kPBytes;
+        const uint32_t va = sbase + C::kVOff + (j % VS) * C::kTileBytes;
+        // MN-major V: 8-key groups at 1024 B (SBO); the second 64-wide column
+        // block (head_dim 128, or the ones block) at LBO
+        const uint32_t lbo = C::kLFromMma ? (sbase + C::kOnesOff - va) : 16384u;
 #pragma unroll
         for (int k = 0; k < kAttnBN / 16; ++k) {
-          // P: K-major, 64-key column blocks of 16 KB; V: MN-major, 8-key
-          // groups at 1024 B (SBO), 64-wide head-dim blocks at 16 KB (LBO).
-          const uint64_t ad = smem_desc_sw128(pb + (k >> 2) * (kAttnBM * 128) + (k & 3) * 32, 16, 1024);
-          const uint64_t bd = smem_desc_sw128(vb + k * 2048, kAttnBN * 128, 1024);
-          umma_f16_ss(tm_o0 + (j & 1) * HD, ad, bd, idesc_o, k > 0 ? 1u : 0u);
+          umma_f16_ss(tmem_base + C::kTmO + t * 128,
+                      smem_desc_sw128(pa + (k >> 2) * 16384 + (k & 3) * 32, 16, 1024),
+                      smem_desc_sw128(va + k * 2048, lbo, 1024), idesc_o, (j > 0 || k > 0) ? 1u : 0u);
         }
-        umma_commit(&o_full[j & 1]);
-        umma_commit(&kv_empty[s]);
-        umma_commit(&p_free[j & 1]);
+        umma_commit(&o_full[t]);
+      };
+      bool ok = mbar_wait(q_full, 0, p.status, kDevTimeoutMma) &&
+                mbar_wait(&k_full[0], 0, p.status, kDevTimeoutMma);
+      if (ok) {
+        tc_fence_after();
+        for (int t = 0; t < kAttnTiles; ++t)
+          if (nblk[t] > 0) issue_s(t, 0);
+        umma_commit(&k_empty[0]);
+      }
+      for (int j = 0; j < nmax && ok; ++j) {
+        if (j + 1 < nmax) {
+          const int s = (j + 1) % KS;
+          if (!(ok = mbar_wait(&k_full[s], ((j + 1) / KS) & 1, p.status, kDevTimeoutMma))) break;
+          for (int t = 0; t < kAttnTiles && ok; ++t) {
+            if (j + 1 < nblk[t]) {
+              if (!(ok = mbar_wait(&s_free[t], j & 1, p.status, kDevTimeoutMma))) break;
+              tc_fence_after();
+              issue_s(t, j + 1);
+            }
+          }
+          if (!ok) break;
+          umma_commit(&k_empty[s]);
+        }
+        if (!(ok = mbar_wait(&v_full[j % VS], (j / VS) & 1, p.status, kDevTimeoutMma))) break;
+        for (int t = 0; t < kAttnTiles && ok; ++t) {
+          if (j < nblk[t]) {
+            if (!(ok = mbar_wait(&p_full[t], j & 1, p.status, kDevTimeoutMma))) break;
+            tc_fence_after();
+            issue_pv(t, j);
+          }
+        }
+        if (!ok) break;
+        umma_commit(&v_empty[j % VS]);
       }
       umma_commit(drain);
       mbar_wait(drain, 0, p.status, kDevTimeoutDrain);
     }
+  }
   } else {
-    // ---------------- softmax / correction / epilogue (warps 2..5) -------------
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsHigh));
+    // ---------------- softmax (warps 4..11) ----------------
+    const int t = (warp - 4) >> 2;
     const int quarter = warp & 3;
-    const int r = quarter * 32 + lane;  // query row within the tile
+    const int r = quarter * 32 + lane;  // row within the tile
+    const int row = q0 + t * kAttnBM + r;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
-    const long long q_glob = p.q_pos0 + q0 + r;
-    const bool causal = (p.flags & TF_ATTN_CAUSAL) != 0;
+    const uint32_t tm_s = tmem_base + lane_off + C::kTmS + t * 128;
+    const uint32_t tm_o = tmem_base + lane_off + C::kTmO + t * 128;
+    const long long q_glob = p.q_pos0 + row;
     const uint8_t* kvalid = p.key_valid ? p.key_valid + static_cast<long long>(b) * p.seq_k : nullptr;
-    uint8_t* pbase = smem + L::kPOff;
+    uint8_t* prow = smem + C::kPOff + t * C::kPBytes + r * 128;
+    const int nb = nblk[t];
+    const float c = p.scale_log2;
 
-    float o_acc[HD];
-#pragma unroll
-    for (int i = 0; i < HD; ++i) o_acc[i] = 0.f;
-    float m2 = -INFINITY;  // running max in the scaled log2 domain
-    float l = 0.f;
-    float alpha_prev = 0.f;
+    float m_ref = -INFINITY;  // reference max (scaled log2 domain)
+    float l = 0.f;            // row sum (when not produced by the MMA)
     bool ok = true;
 
-    auto fold = [&](int jb, float alpha) -> bool {
-      if (!mbar_wait(&o_full[jb & 1], (jb >> 1) & 1, p.status, kDevTimeoutSoftmax)) return false;
+    for (int j = 0; j < nb; ++j) {
+      if (!(ok = mbar_wait(&s_full[t], j & 1, p.status, kDevTimeoutSoftmax))) break;
       tc_fence_after();
-#pragma unroll
-      for (int c = 0; c < HD / 32; ++c) {
+      float s[128];
+      {
         uint32_t v[32];
-        tmem_ld32(tm_o0 + lane_off + (jb & 1) * HD + c * 32, v);
-        tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) o_acc[c * 32 + i] = o_acc[c * 32 + i] * alpha + __uint_as_float(v[i]);
-      }
-      tc_fence_before();
-      mbar_arrive(&o_free[jb & 1]);
-      return true;
-    };
-
-    for (int j = 0; j < n_blocks; ++j) {
-      if (!mbar_wait(&s_full[j & 1], (j >> 1) & 1, p.status, kDevTimeoutSoftmax)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      const uint32_t s_addr = tm_s0 + lane_off + (j & 1) * 128;
-      const long long kbase = static_cast<long long>(j) * kAttnBN;
-      // keys of this block that need masking at all
-      const bool need_mask = kvalid != nullptr || kbase + kAttnBN > p.seq_k ||
-                             (causal && p.k_pos0 + kbase + kAttnBN - 1 > p.q_pos0 + q0);
-      // pass 1: row max
-      float mj = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t v[32];
-        tmem_ld32(s_addr + c * 32, v);
-        tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          float t = __uint_as_float(v[i]) * p.scale_log2;
-          if (need_mask) {
-            const long long kk = kbase + c * 32 + i;
-            bool bad = kk >= p.seq_k;
-            if (causal) bad |= (p.k_pos0 + kk > q_glob);
-            if (kvalid != nullptr && !bad) bad |= kvalid[kk] == 0;
-            t = bad ? -INFINITY : t;
-          }
-          mj = fmaxf(mj, t);
-        }
-      }
-      const float m_new = fmaxf(m2, mj);
-      const float m_use = m_new == -INFINITY ? 0.f : m_new;
-      const float alpha = (m2 == -INFINITY) ? 0.f : exp2f(m2 - m_use);
-      // P buffer j%2 must be free (PV of block j-2 done)
-      if (!mbar_wait(&p_free[j & 1], ((j >> 1) & 1) ^ 1, p.status, kDevTimeoutSoftmax)) {
-        ok = false;
-        break;
-      }
-      // pass 2: probabilities -> fp16 -> swizzled shared memory, row sum
-      float rs = 0.f;
-      uint8_t* prow = pbase + (j & 1) * L::kPBytes + r * 128;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t v[32];
-        tmem_ld32(s_addr + c * 32, v);
-        tmem_wait_ld();
-        uint32_t packed[16];
-#pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          float t0 = __uint_as_float(v[i]) * p.scale_log2;
-          float t1 = __uint_as_float(v[i + 1]) * p.scale_log2;
-          if (need_mask) {
-            const long long k0 = kbase + c * 32 + i;
-            bool bad0 = k0 >= p.seq_k, bad1 = k0 + 1 >= p.seq_k;
-            if (causal) {
-              bad0 |= (p.k_pos0 + k0 > q_glob);
-              bad1 |= (p.k_pos0 + k0 + 1 > q_glob);
-            }
-            if (kvalid != nullptr) {
-              if (!bad0) bad0 |= kvalid[k0] == 0;
-              if (!bad1) bad1 |= kvalid[k0 + 1] == 0;
-            }
-            t0 = bad0 ? -INFINITY : t0;
-            t1 = bad1 ? -INFINITY : t1;
-          }
-          const __half2 ph = __floats2half2_rn(exp2f(t0 - m_use), exp2f(t1 - m_use));
-          const float2 pf = __half22float2(ph);
-          rs += pf.x + pf.y;
-          packed[i >> 1] = *reinterpret_cast<const uint32_t*>(&ph);
-        }
-        // 32 keys = 4 chunks of 16 B; chunk index within the 64-key block
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          const int chunk = c * 4 + q;       // 0..15 over the 128 keys
-          const int blk = chunk >> 3;        // 64-key column block
-          const int cc = (chunk & 7) ^ (r & 7);
-          *reinterpret_cast<uint4*>(prow + blk * (kAttnBM * 128) + cc * 16) =
-              make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+          tmem_ld32(tm_s + q * 32, v);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) s[q * 32 + i] = __uint_as_float(v[i]);
         }
       }
       tc_fence_before();
-      mbar_arrive(&s_free[j & 1]);
-      fence_proxy_async_smem();
-      mbar_arrive(&p_full[j & 1]);
-      l = l * alpha + rs;
-      m2 = m_new;
-      if (j >= 1) {
-        if (!fold(j - 1, alpha_prev)) {
-          ok = false;
-          break;
+      mbar_arrive(&s_free[t]);
+
+      // ---- masking (tails, causal diagonal, key padding) ----
+      const long long kbase = static_cast<long long>(j) * kAttnBN;
+      long long lim_ll = p.seq_k - kbase;
+      if (causal) {
+        const long long cl = q_glob - p.k_pos0 - kbase + 1;
+        lim_ll = cl < lim_ll ? cl : lim_ll;
+      }
+      const int lim = lim_ll < 0 ? 0 : (lim_ll > kAttnBN ? kAttnBN : static_cast<int>(lim_ll));
+      if (__any_sync(0xffffffffu, lim < kAttnBN)) {
+#pragma unroll
+        for (int i = 0; i < 128; ++i) s[i] = i < lim ? s[i] : -INFINITY;
+      }
+      if (kvalid != nullptr) {
+        const uint8_t* kv = kvalid + kbase;
+        const long long rem = p.seq_k - kbase;
+        const int avail = rem >= kAttnBN ? kAttnBN : static_cast<int>(rem);
+        const bool fast = avail == kAttnBN && (reinterpret_cast<uintptr_t>(kv) & 15) == 0;
+#pragma unroll
+        for (int g = 0; g < 128; g += 16) {
+          uint32_t w[4] = {0u, 0u, 0u, 0u};
+          if (fast) {
+            const uint4 q4 = __ldg(reinterpret_cast<const uint4*>(kv + g));
+            w[0] = q4.x;
+            w[1] = q4.y;
+            w[2] = q4.z;
+            w[3] = q4.w;
+          } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              if (g + i < avail) w[i >> 2] |= static_cast<uint32_t>(kv[g + i]) << (8 * (i & 3));
+          }
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            if (((w[i >> 2] >> (8 * (i & 3))) & 0xffu) == 0u) s[g + i] = -INFINITY;
         }
       }
-      alpha_prev = alpha;
+
+      // ---- row max (tree) ----
+      float mx[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) mx[i] = fmaxf(fmaxf(s[i], s[i + 16]), fmaxf(s[i + 32], s[i + 48]));
+#pragma unroll
+      for (int i = 0; i < 16; ++i) mx[i] = fmaxf(mx[i], fmaxf(fmaxf(s[i + 64], s[i + 80]), fmaxf(s[i + 96], s[i + 112])));
+#pragma unroll
+      for (int w = 8; w > 0; w >>= 1)
+#pragma unroll
+        for (int i = 0; i < w; ++i) mx[i] = fmaxf(mx[i], mx[i + w]);
+      const float m_row = mx[0] * c;
+
+      // ---- lazy rescale of O (and l) ----
+      const bool need = m_row > m_ref + kRescaleThreshold;
+      if (j == 0) {
+        m_ref = m_row;
+      } else if (__any_sync(0xffffffffu, need)) {
+        const float m_new = fmaxf(m_ref, m_row);
+        const float alpha = m_ref == -INFINITY ? 0.f : ex2_f32(m_ref - m_new);
+        if (!(ok = mbar_wait(&o_full[t], (j - 1) & 1, p.status, kDevTimeoutSoftmax))) break;
+        tc_fence_after();
+        rescale_o<C::kNO>(tm_o, alpha);
+        l *= alpha;
+        m_ref = m_new;
+      }
+      const float m_use = m_ref == -INFINITY ? 0.f : m_ref;
+
+      // ---- probabilities -> fp16 pairs (and the row sum) ----
+      uint32_t pk[64];
+      float ls[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int i = 0; i < 64; ++i) {
+        const float a0 = fmaf(s[2 * i], c, -m_use);
+        const float a1 = fmaf(s[2 * i + 1], c, -m_use);
+        if constexpr (EXP16) {
+          pk[i] = ex2_pair_f16(a0, a1);
+          if constexpr (!C::kLFromMma) {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&pk[i]));
+            ls[i & 7] += f.x + f.y;
+          }
+        } else {
+          const float e0 = ex2_f32(a0), e1 = ex2_f32(a1);
+          pk[i] = pack_f16x2_rn(e0, e1);
+          if constexpr (!C::kLFromMma) ls[i & 7] += e0 + e1;
+        }
+      }
+      if constexpr (!C::kLFromMma) l += ((ls[0] + ls[1]) + (ls[2] + ls[3])) + ((ls[4] + ls[5]) + (ls[6] + ls[7]));
+
+      // P buffer is free once PV of block j-1 has completed
+      if (j > 0) {
+        if (!(ok = mbar_wait(&o_full[t], (j - 1) & 1, p.status, kDevTimeoutSoftmax))) break;
+      }
+#pragma unroll
+      for (int ch = 0; ch < 16; ++ch) {
+        const int blk = ch >> 3;
+        const int cc = (ch & 7) ^ (r & 7);
+        *reinterpret_cast<uint4*>(prow + blk * 16384 + cc * 16) =
+            make_uint4(pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]);
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&p_full[t]);
     }
-    if (ok && n_blocks > 0) ok = fold(n_blocks - 1, alpha_prev);
 
     // ---------------- epilogue ----------------
-    const int row = q0 + r;
-    if (ok && row < p.seq_q) {
-      const float inv = l > 0.f ? 1.f / l : 0.f;
-      if (p.lse != nullptr) {
-        const float lse = l > 0.f ? (m2 + __log2f(l)) * 0.69314718055994531f : -INFINITY;
-        p.lse[(static_cast<long long>(b) * p.heads + h) * p.seq_q + row] = lse;
-      }
-      const long long obase = static_cast<long long>(b) * p.bs_o + static_cast<long long>(row) * p.ld_o + h * HD;
-      if (p.flags & TF_ATTN_OUT_F32) {
-        float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + obase);
+    if (ok) {
+      float inv = 0.f;
+      uint32_t ov[C::kNO];
+      if (nb > 0) {
+        if (!(ok = mbar_wait(&o_full[t], (nb - 1) & 1, p.status, kDevTimeoutSoftmax))) {
+          // fall through to the barrier; nothing is written
+        } else {
+          tc_fence_after();
 #pragma unroll
-        for (int i = 0; i < HD / 4; ++i)
-          dst[i] = make_float4(o_acc[4 * i] * inv, o_acc[4 * i + 1] * inv, o_acc[4 * i + 2] * inv,
-                               o_acc[4 * i + 3] * inv);
+          for (int q = 0; q < C::kNO / 32; ++q) {
+            uint32_t v[32];
+            tmem_ld32(tm_o + q * 32, v);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) ov[q * 32 + i] = v[i];
+          }
+          if constexpr (C::kNO % 32 == 16) {
+            uint32_t v[16];
+            tmem_ld16(tm_o + (C::kNO / 32) * 32, v);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 16; ++i) ov[(C::kNO / 32) * 32 + i] = v[i];
+          }
+          if constexpr (C::kLFromMma) l = __uint_as_float(ov[HD]);
+        }
       } else {
-        uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(p.out) + obase);
 #pragma unroll
-        for (int i = 0; i < HD / 8; ++i)
-          dst[i] = make_uint4(pack_half2(o_acc[8 * i] * inv, o_acc[8 * i + 1] * inv),
-                              pack_half2(o_acc[8 * i + 2] * inv, o_acc[8 * i + 3] * inv),
-                              pack_half2(o_acc[8 * i + 4] * inv, o_acc[8 * i + 5] * inv),
-                              pack_half2(o_acc[8 * i + 6] * inv, o_acc[8 * i + 7] * inv));
+        for (int i = 0; i < C::kNO; ++i) ov[i] = 0u;
+      }
+      if (ok && row < p.seq_q) {
+        inv = l > 0.f ? 1.f / l : 0.f;
+        if (p.lse != nullptr)
+          p.lse[(static_cast<long long>(b) * p.heads + h) * p.seq_q + row] =
+              l > 0.f ? (m_ref + __log2f(l)) * 0.69314718055994531f : -INFINITY;
+        const long long obase =
+            static_cast<long long>(b) * p.bs_o + static_cast<long long>(row) * p.ld_o + h * HD;
+        if (p.flags & TF_ATTN_OUT_F32) {
+          float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + obase);
+#pragma unroll
+          for (int i = 0; i < HD / 4; ++i)
+            dst[i] = make_float4(__uint_as_float(ov[4 * i]) * inv, __uint_as_float(ov[4 * i + 1]) * inv,
+                                 __uint_as_float(ov[4 * i + 2]) * inv, __uint_as_float(ov[4 * i + 3]) * inv);
+        } else {
+          uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(p.out) + obase);
+#pragma unroll
+          for (int i = 0; i < HD / 8; ++i)
+            dst[i] = make_uint4(
+                pack_half2(__uint_as_float(ov[8 * i]) * inv, __uint_as_float(ov[8 * i + 1]) * inv),
+                pack_half2(__uint_as_float(ov[8 * i + 2]) * inv, __uint_as_float(ov[8 * i + 3]) * inv),
+                pack_half2(__uint_as_float(ov[8 * i + 4]) * inv, __uint_as_float(ov[8 * i + 5]) * inv),
+                pack_half2(__uint_as_float(ov[8 * i + 6]) * inv, __uint_as_float(ov[8 * i + 7]) * inv));
+        }
       }
     }
   }
@@ -390,15 +568,14 @@ __global__ void attn_merge_kernel(float* __restrict__ o_acc, float* __restrict__
   // one warp per (b, h, row); lanes stride over head_dim
   const long long gw = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
-  const long long rows = static_cast<long long>(gridDim.y) * heads * seq_q;  // gridDim.y = batch
-  (void)rows;
   const int b = blockIdx.y;
   if (gw >= static_cast<long long>(heads) * seq_q) return;
   const int h = static_cast<int>(gw / seq_q);
   const int i = static_cast<int>(gw % seq_q);
   const long long li = (static_cast<long long>(b) * heads + h) * seq_q + i;
   const float la = lse_acc[li], lb = lse_part[li];
-  const float L = fmaxf(la, lb) == -INFINITY ? -INFINITY : fmaxf(la, lb) + log1pf(__expf(-fabsf(la - lb)));
+  const float mx = fmaxf(la, lb);
+  const float L = mx == -INFINITY ? -INFINITY : mx + log1pf(__expf(-fabsf(la - lb)));
   const float wa = la == -INFINITY ? 0.f : __expf(la - L);
   const float wb = lb == -INFINITY ? 0.f : __expf(lb - L);
   const long long base = static_cast<long long>(b) * bs + static_cast<long long>(i) * ld + static_cast<long long>(h) * hd;
@@ -415,20 +592,29 @@ __global__ void attn_merge_kernel(float* __restrict__ o_acc, float* __restrict__
 // host side
 // ---------------------------------------------------------------------------
 
-template <int HD>
+template <int HD, bool EXP16>
 static int launch_flash(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                         const AttnKParams& kp, dim3 grid, cudaStream_t stream) {
-  using L = AttnSmem<HD>;
-  auto kern = flash_fwd_tcgen05<HD>;
+  using C = AttnCfg<HD>;
+  auto kern = flash_fwd_tcgen05<HD, EXP16>;
   static bool attr_done[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (!attr_done[dev & 63]) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
+    // The in-kernel register split assumes the launch pool of exactly
+    // kRegsLaunch registers per thread; refuse anything else rather than
+    // risk a split that can never be satisfied.
+    cudaFuncAttributes fa;
+    cudaError_t e = cudaFuncGetAttributes(&fa, kern);
+    if (e != cudaSuccess) return set_error(TF_ERR_LAUNCH, "cudaFuncGetAttributes(flash): %s", cudaGetErrorString(e));
+    if (fa.numRegs != kRegsLaunch)
+      return set_error(TF_ERR_LAUNCH, "flash kernel built with %d registers/thread, expected %d", fa.numRegs,
+                       kRegsLaunch);
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kAlloc);
     if (e != cudaSuccess) return set_error(TF_ERR_LAUNCH, "cudaFuncSetAttribute(flash): %s", cudaGetErrorString(e));
     attr_done[dev & 63] = true;
   }
-  kern<<<grid, kAttnThreads, L::kAlloc, stream>>>(tq, tk, tv, kp);
+  kern<<<grid, kAttnThreads, C::kAlloc, stream>>>(tq, tk, tv, kp);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(TF_ERR_LAUNCH, "flash launch: %s", cudaGetErrorString(e));
   return TF_OK;
@@ -470,16 +656,20 @@ int flash_fwd(const AttnArgs& a, cudaStream_t stream) {
   kp.heads = static_cast<int>(a.heads);
   kp.seq_q = static_cast<int>(a.seq_q);
   kp.seq_k = static_cast<int>(a.seq_k);
-  kp.q_tiles = static_cast<int>((a.seq_q + kAttnBM - 1) / kAttnBM);
+  kp.q_blocks = static_cast<int>((a.seq_q + kAttnBM * kAttnTiles - 1) / (kAttnBM * kAttnTiles));
   kp.scale_log2 = a.scale * 1.4426950408889634f;
   kp.q_pos0 = a.q_pos0;
   kp.k_pos0 = a.k_pos0;
   kp.flags = a.flags;
   kp.status = device_status_ptr();
   if (kp.status == nullptr) return last_error_code();
-  dim3 grid(kp.q_tiles, static_cast<unsigned>(a.heads), static_cast<unsigned>(a.batch));
-  return a.head_dim == 64 ? launch_flash<64>(tq, tk, tv, kp, grid, stream)
-                          : launch_flash<128>(tq, tk, tv, kp, grid, stream);
+  dim3 grid(kp.q_blocks, static_cast<unsigned>(a.heads), static_cast<unsigned>(a.batch));
+  const bool exp16 = !(a.flags & TF_ATTN_EXP_F32);
+  if (a.head_dim == 64)
+    return exp16 ? launch_flash<64, true>(tq, tk, tv, kp, grid, stream)
+                 : launch_flash<64, false>(tq, tk, tv, kp, grid, stream);
+  return exp16 ? launch_flash<128, true>(tq, tk, tv, kp, grid, stream)
+               : launch_flash<128, false>(tq, tk, tv, kp, grid, stream);
 }
 
 int attn_merge(const MergeArgs& a, cudaStream_t stream) {

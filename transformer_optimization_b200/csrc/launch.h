@@ -34,9 +34,26 @@ int make_tmap_3d_f16(CUtensorMap* map, const void* base, long long inner, long l
                      long long ld, long long bstride, int box_inner, int box_rows);
 
 // kernels (defined in their own translation units)
-int gemm_f16(const void* A, long long lda, const void* W, long long ldw, const void* bias, void* C,
-             long long ldc, long long M, long long N, long long K, int epilogue, int force_bn,
-             cudaStream_t stream);
+struct GemmCall {
+  const void* A;
+  long long lda;
+  const void* W;
+  long long ldw;
+  const float* bias;
+  void* C;  // fp16 output (epilogues 0, 1)
+  long long ldc;
+  const float* x_in;  // fp32 residual (epilogue 2)
+  float* x_out;
+  long long ldx;
+  const uint8_t* valid;
+  int mask_mode;
+  long long M, N, K;
+  int epilogue;
+  int a_repeat;
+  int tile_n;
+};
+
+int gemm_f16(const GemmCall& g, cudaStream_t stream);
 
 int ln_residual(const float* x, const void* delta, const float* w, const float* b, float eps,
                 const uint8_t* valid, long long M, int D, int flags, float* x_out, void* normed,

@@ -73,25 +73,45 @@ def ln_residual(x: torch.Tensor, delta: Optional[torch.Tensor], weight: torch.Te
     return (x_out if write_x else x), normed
 
 
-def linear(a: torch.Tensor, w: torch.Tensor, b: torch.Tensor, *, gelu: bool = False,
-           out: Optional[torch.Tensor] = None, tile_n: int = 0) -> torch.Tensor:
-    """fp16 GEMM on tcgen05 (tf_gemm): out = [gelu](a @ w.T + b), a [..., K]
-    fp16 with unit inner stride, w [N, K] fp16, b [N] fp16."""
-    _need_cuda("linear", a, w, b, out)
-    if a.dtype != torch.float16 or w.dtype != torch.float16 or b.dtype != torch.float16:
-        raise ValueError("linear: a, w and b must be fp16")
+def _gemm_operands(name, a, w, b, w_split):
+    _need_cuda(name, a, w, b)
+    if a.dtype != torch.float16 or w.dtype != torch.float16:
+        raise ValueError(f"{name}: a and w must be fp16")
+    if b.dtype != torch.float32 or not b.is_contiguous():
+        raise ValueError(f"{name}: bias must be contiguous fp32")
     k = a.shape[-1]
     n = w.shape[0]
+    if w.shape[1] != (2 * k if w_split else k) or b.numel() != n:
+        raise ValueError(f"{name}: weight must be [N, {'2K' if w_split else 'K'}] and bias [N]")
     a2 = a.reshape(-1, k)
-    if a2.stride(-1) != 1 or w.stride(-1) != 1 or not b.is_contiguous():
-        raise ValueError("linear: operands need a unit inner stride")
+    if a2.stride(-1) != 1 or w.stride(-1) != 1:
+        raise ValueError(f"{name}: operands need a unit inner stride")
+    return a2, n, k
+
+
+def split_weight(w: torch.Tensor) -> torch.Tensor:
+    """[N, K] fp32 weight -> [N, 2K] fp16 [W_hi | W_lo] with W_hi = fp16(W),
+    W_lo = fp16(W - W_hi): the pair represents W to ~2^-22 relative."""
+    w = w.detach().float()
+    hi = w.half()
+    lo = (w - hi.float()).half()
+    return torch.cat([hi, lo], dim=1).contiguous()
+
+
+def linear(a: torch.Tensor, w: torch.Tensor, b: torch.Tensor, *, gelu: bool = False,
+           out: Optional[torch.Tensor] = None, tile_n: int = 0, w_split: bool = False) -> torch.Tensor:
+    """fp16 GEMM on tcgen05 (tf_gemm): out = fp16([gelu](a @ w.T + b)), a
+    [..., K] fp16 with unit inner stride, w [N, K] fp16 (or split_weight's
+    [N, 2K] with w_split), b [N] fp32."""
+    a2, n, k = _gemm_operands("linear", a, w, b, w_split)
+    _need_cuda("linear", out)
     m = a2.shape[0]
     if out is None:
         out = torch.empty(*a.shape[:-1], n, dtype=torch.float16, device=a.device)
     o2 = out.view(-1, n) if out.is_contiguous() else out
-    if o2.stride(-1) != 1:
-        raise ValueError("linear: out needs a unit inner stride")
-    epi = _abi.TF_EPI_BIAS_GELU if gelu else _abi.TF_EPI_BIAS
+    if o2.stride(-1) != 1 or o2.dtype != torch.float16:
+        raise ValueError("linear: out must be fp16 with a unit inner stride")
+    epi = (_abi.TF_EPI_BIAS_GELU if gelu else _abi.TF_EPI_BIAS) | (_abi.TF_EPI_W_SPLIT if w_split else 0)
     if tile_n:
         _abi.call("tf_gemm_tiled", _ptr(a2), a2.stride(0), _ptr(w), w.stride(0), _ptr(b), _ptr(o2), o2.stride(0),
                   m, n, k, epi, tile_n, _stream())
@@ -101,10 +121,39 @@ def linear(a: torch.Tensor, w: torch.Tensor, b: torch.Tensor, *, gelu: bool = Fa
     return out
 
 
+def linear_residual(a: torch.Tensor, w: torch.Tensor, b: torch.Tensor, x_in: torch.Tensor,
+                    x_out: Optional[torch.Tensor] = None, valid: Optional[torch.Tensor] = None, *,
+                    mask_delta: bool = False, mask_x: bool = False, w_split: bool = False) -> torch.Tensor:
+    """GEMM closing a residual connection in fp32 (tf_gemm_residual):
+    x_out = mask_x(x_in + mask_delta(a @ w.T + b)). x_in/x_out fp32 [..., N]
+    contiguous (x_out may be x_in); valid bool/uint8 [rows] for the masks."""
+    a2, n, k = _gemm_operands("linear_residual", a, w, b, w_split)
+    _need_cuda("linear_residual", x_in, x_out, valid)
+    if x_in.dtype != torch.float32 or not x_in.is_contiguous() or x_in.shape[-1] != n:
+        raise ValueError("linear_residual: x_in must be contiguous fp32 [..., N]")
+    if x_out is None:
+        x_out = torch.empty_like(x_in)
+    if x_out.shape != x_in.shape or x_out.dtype != torch.float32 or not x_out.is_contiguous():
+        raise ValueError("linear_residual: x_out must match x_in")
+    m = a2.shape[0]
+    if x_in.numel() // n != m:
+        raise ValueError("linear_residual: row count of a and x differ")
+    if mask_delta and mask_x:
+        raise ValueError("linear_residual: one mask mode at a time")
+    mode = _abi.TF_RES_MASK_DELTA if mask_delta else (_abi.TF_RES_MASK_X if mask_x else _abi.TF_RES_NO_MASK)
+    if mode and (valid is None or valid.numel() != m or valid.dtype not in (torch.bool, torch.uint8)):
+        raise ValueError("linear_residual: masking needs a bool/uint8 mask with one entry per row")
+    if valid is not None and not valid.is_contiguous():
+        valid = valid.contiguous()
+    _abi.call("tf_gemm_residual", _ptr(a2), a2.stride(0), _ptr(w), w.stride(0), _ptr(b), _ptr(x_in), _ptr(x_out), n,
+              _ptr(valid) if mode else None, mode, m, n, k, 1 if w_split else 0, _stream())
+    return x_out
+
+
 def flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, heads: int, scale: float, *,
                     causal: bool = False, key_valid: Optional[torch.Tensor] = None, q_pos0: int = 0,
                     k_pos0: int = 0, out: Optional[torch.Tensor] = None, out_dtype: torch.dtype = torch.float16,
-                    lse: Optional[torch.Tensor] = None, want_lse: bool = False):
+                    lse: Optional[torch.Tensor] = None, want_lse: bool = False, exp_f32: bool = False):
     """Flash attention forward (tf_flash_fwd).
 
     q: [B, Sq, H*hd] fp16 view with unit inner stride (may be a column slice
@@ -133,6 +182,8 @@ def flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, heads: in
             raise ValueError("flash_attention: key_valid must be bool [B, Sk]")
         key_valid = key_valid.contiguous()
     flags = (_abi.TF_ATTN_CAUSAL if causal else 0) | (_abi.TF_ATTN_OUT_F32 if out_dtype == torch.float32 else 0)
+    if exp_f32:
+        flags |= _abi.TF_ATTN_EXP_F32
     _abi.call("tf_flash_fwd", _ptr(q), _ptr(k), _ptr(v), q.stride(1), k.stride(1), q.stride(0), k.stride(0),
               _ptr(out), out.stride(1), out.stride(0), _ptr(lse), _ptr(key_valid), bsz, heads, sq, sk, hd,
               float(scale), int(q_pos0), int(k_pos0), flags, _stream())

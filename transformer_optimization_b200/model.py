@@ -102,22 +102,26 @@ def copy_model_weights(baseline: nn.Module, optimized: nn.Module, strict: bool =
 
 
 class _LayerWeights:
-    """fp16 copies of one layer's GEMM operands; packed [3D, D] QKV
-    (torch_transformer_benchmark.py:440-504)."""
+    """GEMM operands of one layer: fp16 weights (packed [3D, D] QKV, as the
+    reference packs them: torch_transformer_benchmark.py:440-504) and fp32
+    biases. With `split_ffn_out` the FFN-out weight is kept as [W_hi | W_lo]
+    (kernels.split_weight) for a near-fp32 product."""
 
-    __slots__ = ("wqkv", "bqkv", "wo", "bo", "w1", "b1", "w2", "b2")
+    __slots__ = ("wqkv", "bqkv", "wo", "bo", "w1", "b1", "w2", "b2", "split_w2")
 
-    def __init__(self, blk: BaselineTransformerBlock) -> None:
+    def __init__(self, blk: BaselineTransformerBlock, split_ffn_out: bool) -> None:
         at = blk.attention
         with torch.no_grad():
             self.wqkv = torch.cat([at.q_proj.weight, at.k_proj.weight, at.v_proj.weight], 0).half().contiguous()
-            self.bqkv = torch.cat([at.q_proj.bias, at.k_proj.bias, at.v_proj.bias], 0).half().contiguous()
+            self.bqkv = torch.cat([at.q_proj.bias, at.k_proj.bias, at.v_proj.bias], 0).float().contiguous()
             self.wo = at.out_proj.weight.half().contiguous()
-            self.bo = at.out_proj.bias.half().contiguous()
+            self.bo = at.out_proj.bias.float().contiguous()
             self.w1 = blk.ffn_in.weight.half().contiguous()
-            self.b1 = blk.ffn_in.bias.half().contiguous()
-            self.w2 = blk.ffn_out.weight.half().contiguous()
-            self.b2 = blk.ffn_out.bias.half().contiguous()
+            self.b1 = blk.ffn_in.bias.float().contiguous()
+            self.split_w2 = split_ffn_out
+            self.w2 = (kernels.split_weight(blk.ffn_out.weight) if split_ffn_out
+                       else blk.ffn_out.weight.half().contiguous())
+            self.b2 = blk.ffn_out.bias.float().contiguous()
 
 
 class _GraphCacheEntry:
@@ -155,14 +159,24 @@ class UserOptimizedTransformer(BaselineTransformer):
         self._graph_pool = None
         self._mask_all_true_cache: Dict[Tuple, bool] = {}
         self.use_cuda_graphs = True
+        # FFN-out with split (hi/lo fp16) weights: twice that GEMM's tensor
+        # work for a near-fp32 weight. None = automatic (deep stacks only,
+        # where fp16 weight rounding accumulates over many residual adds).
+        self.precise_ffn_out: Optional[bool] = None
+
+    def _split_ffn_out(self) -> bool:
+        if self.precise_ffn_out is not None:
+            return bool(self.precise_ffn_out)
+        return self.config.num_layers >= 16
 
     # ------------------------------------------------------------------ caches
     def _layer_weights(self) -> list:
         """fp16 weight caches, rebuilt whenever a source parameter's storage,
         dtype or device changes (torch_transformer_benchmark.py:452-466)."""
-        key = tuple((p.data_ptr(), p.dtype, p.device, p._version) for p in self.parameters())
+        split = self._split_ffn_out()
+        key = tuple((p.data_ptr(), p.dtype, p.device, p._version) for p in self.parameters()) + (split,)
         if self._weights is None or key != self._weights_key:
-            self._weights = [_LayerWeights(blk) for blk in self.layers]
+            self._weights = [_LayerWeights(blk, split) for blk in self.layers]
             self._weights_key = key
             self._graph_cache.clear()
         return self._weights
@@ -186,15 +200,15 @@ class UserOptimizedTransformer(BaselineTransformer):
     # ------------------------------------------------------------------ core
     def _forward_core(self, x: torch.Tensor, valid: Optional[torch.Tensor], mask_active: bool) -> torch.Tensor:
         """The per-layer schedule of torch_transformer_benchmark.py:4003-4326
-        (fp16-GEMM branch 4130-4199) with the "pending residual": each
-        sub-block's output is added by the next LayerNorm site. No host sync,
-        so it is safe to capture."""
+        (fp16-GEMM branch 4130-4199). The residual adds of the reference's
+        LayerNorm sites happen in the epilogues of out_proj and ffn_out
+        (fp32, same masking points: mask_delta after attention, mask_x after
+        the FFN); the LayerNorm kernels then only normalise. No host sync, so
+        it is safe to capture."""
         cfg = self.config
         b, s, d = x.shape
-        m = b * s
         h = cfg.num_heads
-        hd = d // h
-        scale = hd ** -0.5
+        scale = (d // h) ** -0.5
         wts = self._layer_weights()
         vflat = valid.reshape(-1) if mask_active else None
         kvalid = valid if mask_active else None
@@ -204,32 +218,23 @@ class UserOptimizedTransformer(BaselineTransformer):
         normed = torch.empty(b, s, d, dtype=torch.float16, device=dev)
         qkv = torch.empty(b, s, 3 * d, dtype=torch.float16, device=dev)
         ctx = torch.empty(b, s, d, dtype=torch.float16, device=dev)
-        delta = torch.empty(b, s, d, dtype=torch.float16, device=dev)
         hidden = torch.empty(b, s, cfg.ffn_dim, dtype=torch.float16, device=dev)
 
         cur = x  # residual stream; the caller's x is read, never written
-        pending = None
         for li, blk in enumerate(self.layers):
             w = wts[li]
-            # closes the previous FFN residual (+ the block's trailing mask)
-            if pending is None:
-                kernels.ln_residual(cur, None, blk.norm1.weight, blk.norm1.bias, blk.norm1.eps, normed=normed)
-            else:
-                cur, _ = kernels.ln_residual(cur, pending, blk.norm1.weight, blk.norm1.bias, blk.norm1.eps,
-                                             vflat, mask_x=mask_active, write_x=True, x_out=x_res,
-                                             normed=normed)
+            kernels.ln_residual(cur, None, blk.norm1.weight, blk.norm1.bias, blk.norm1.eps, normed=normed)
             kernels.linear(normed, w.wqkv, w.bqkv, out=qkv)
             kernels.flash_attention(qkv[..., :d], qkv[..., d:2 * d], qkv[..., 2 * d:], h, scale,
                                     causal=cfg.causal, key_valid=kvalid, out=ctx)
-            kernels.linear(ctx, w.wo, w.bo, out=delta)
-            cur, _ = kernels.ln_residual(cur, delta, blk.norm2.weight, blk.norm2.bias, blk.norm2.eps, vflat,
-                                         mask_delta=mask_active, write_x=True, x_out=x_res, normed=normed)
+            cur = kernels.linear_residual(ctx, w.wo, w.bo, cur, x_res, vflat, mask_delta=mask_active)
+            kernels.ln_residual(cur, None, blk.norm2.weight, blk.norm2.bias, blk.norm2.eps, normed=normed)
             kernels.linear(normed, w.w1, w.b1, gelu=True, out=hidden)
-            kernels.linear(hidden, w.w2, w.b2, out=delta)
-            pending = delta
+            kernels.linear_residual(hidden, w.w2, w.b2, cur, x_res, vflat, mask_x=mask_active,
+                                    w_split=w.split_w2)
         fn = self.final_norm
-        _, out = kernels.ln_residual(cur, pending, fn.weight, fn.bias, fn.eps, vflat, mask_x=mask_active,
-                                     mask_out=mask_active, out_dtype=torch.float32)
+        _, out = kernels.ln_residual(cur, None, fn.weight, fn.bias, fn.eps, vflat, mask_out=mask_active,
+                                     out_dtype=torch.float32)
         return out
 
     # ------------------------------------------------------------------ graphs
@@ -280,7 +285,7 @@ class UserOptimizedTransformer(BaselineTransformer):
 
         if not self.use_cuda_graphs or not self._graph_memory_safe(x):
             return self._forward_core(x, valid_token_mask, mask_active)
-        key = (tuple(x.shape), x.device, cfg.causal, mask_kind)
+        key = (tuple(x.shape), x.device, cfg.causal, mask_kind, self._split_ffn_out())
         if key in self._graph_unsupported:
             return self._forward_core(x, valid_token_mask, mask_active)
         self._layer_weights()  # may invalidate cached graphs
