@@ -98,10 +98,11 @@ int tf_ln_residual(const float* x, const void* delta, const float* w, const floa
 int tf_gemm(const void* A, int64_t lda, const void* W, int64_t ldw, const float* bias, void* C, int64_t ldc,
             int64_t M, int64_t N, int64_t K, int epilogue, void* stream);
 
-/* tf_gemm with an explicit N tile (64, 128 or 256; 0 = automatic). For
- * tuning and tests. */
+/* tf_gemm with an explicit tiling, for tuning and tests: tile_n = N tile
+ * (64, 128 or 256; 0 = automatic); pair = 1 one-CTA 128-row tiles, 2 two-SM
+ * 256-row tiles on a CTA pair (tile_n 128 or 256), 0 = automatic. */
 int tf_gemm_tiled(const void* A, int64_t lda, const void* W, int64_t ldw, const float* bias, void* C,
-                  int64_t ldc, int64_t M, int64_t N, int64_t K, int epilogue, int tile_n, void* stream);
+                  int64_t ldc, int64_t M, int64_t N, int64_t K, int epilogue, int tile_n, int pair, void* stream);
 
 /* GEMM whose epilogue closes a residual connection in fp32:
  *   x_out[M, N] = mask_x(x_in + mask_delta(A * W^T + bias))

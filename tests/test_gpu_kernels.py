@@ -111,6 +111,37 @@ def test_gemm_tiles(K, tile_n):
     assert torch.all((out - ref).abs() <= 2e-3 * ref.abs() + 1e-3)
 
 
+@pytest.mark.parametrize("m", [64, 300, 1000, 4096])
+@pytest.mark.parametrize("tile_n", [128, 256])
+@pytest.mark.parametrize("gelu", [False, True])
+def test_gemm_pair_tiles(K, m, tile_n, gelu):
+    """2-SM (CTA pair, cta_group::2) tiles, including row tails that leave
+    the second CTA of a pair partly or fully outside M."""
+    k, n = 1024, 1536
+    a, w, bias = _gemm_inputs(m, k, n, m + tile_n)
+    w16 = w.half()
+    ref = om.linear_fp16(a, w16, bias, gelu)
+    out = K.linear(a.cuda(), w16.cuda(), bias.cuda(), gelu=gelu, tile_n=tile_n, pair=2).float().cpu()
+    err = (out - ref).abs()
+    assert torch.all(err <= 2e-3 * ref.abs() + 1e-3), f"max err {err.max()}"
+
+
+@pytest.mark.parametrize("mode", ["none", "mask_delta", "mask_x"])
+def test_gemm_residual_large(K, mode):
+    """Large enough for the automatic choice to take 2-SM tiles."""
+    m, k, n = 9000, 512, 1024
+    a, w, bias = _gemm_inputs(m, k, n, 77)
+    w16 = w.half()
+    g = torch.Generator().manual_seed(2)
+    x = torch.randn(m, n, generator=g)
+    valid = torch.rand(m, generator=g) > 0.1
+    md, mx = mode == "mask_delta", mode == "mask_x"
+    ref = om.linear_residual(a, w16, bias, x, valid, md, mx)
+    out = K.linear_residual(a.cuda(), w16.cuda(), bias.cuda(), x.cuda(), None, valid.cuda(), mask_delta=md,
+                            mask_x=mx)
+    assert torch.allclose(out.cpu(), ref, atol=1e-4, rtol=1e-5)
+
+
 def test_gemm_strided_output(K):
     """QKV-style: write into a column slice of a wider buffer."""
     m, k, n = 200, 512, 512
@@ -160,8 +191,9 @@ def test_gemm_split_weight(K, k):
     split = K.linear_residual(a.cuda(), K.split_weight(w).cuda(), bias.cuda(), x.cuda(), w_split=True).cpu()
     e_plain = (plain - ref).abs().max().item()
     e_split = (split - ref).abs().max().item()
-    assert e_split < e_plain / 8, (e_split, e_plain)
-    assert torch.allclose(split, ref, atol=1e-4, rtol=1e-5)
+    # what is left is the fp32 accumulation over K products
+    assert e_split < e_plain / 4, (e_split, e_plain)
+    assert torch.allclose(split, ref, atol=1e-4 * math.sqrt(k / 1024), rtol=1e-5)
     # the fp16-output GEMM takes split weights too
     out16 = K.linear(a.cuda(), K.split_weight(w).cuda(), bias.cuda(), w_split=True).float().cpu()
     r16 = ref.half().float()

@@ -156,7 +156,7 @@ static inline int begin_call() {
 
 extern "C" {
 
-int tf_abi_version(void) { return 2; }
+int tf_abi_version(void) { return 3; }
 
 const char* tf_last_error(void) { return tfb::g_msg; }
 
@@ -187,7 +187,8 @@ int tf_ln_residual(const float* x, const void* delta, const float* w, const floa
 }
 
 static int gemm_common(const void* A, int64_t lda, const void* W, int64_t ldw, const float* bias, void* C,
-                       int64_t ldc, int64_t M, int64_t N, int64_t K, int epilogue, int tile_n, void* stream) {
+                       int64_t ldc, int64_t M, int64_t N, int64_t K, int epilogue, int tile_n, int pair,
+                       void* stream) {
   if (epilogue & ~(0xF | TF_EPI_W_SPLIT)) return set_error(TF_ERR_SHAPE, "tf_gemm: unknown epilogue bits");
   tfb::GemmCall g = {};
   g.A = A;
@@ -204,6 +205,7 @@ static int gemm_common(const void* A, int64_t lda, const void* W, int64_t ldw, c
   if (g.epilogue > 1) return set_error(TF_ERR_SHAPE, "tf_gemm: epilogue %d", g.epilogue);
   g.a_repeat = (epilogue & TF_EPI_W_SPLIT) ? 2 : 1;
   g.tile_n = tile_n;
+  g.pair = pair;
   return tfb::gemm_f16(g, as_stream(stream));
 }
 
@@ -211,17 +213,19 @@ int tf_gemm(const void* A, int64_t lda, const void* W, int64_t ldw, const float*
             int64_t M, int64_t N, int64_t K, int epilogue, void* stream) {
   int rc = begin_call();
   if (rc) return rc;
-  return gemm_common(A, lda, W, ldw, bias, C, ldc, M, N, K, epilogue, 0, stream);
+  return gemm_common(A, lda, W, ldw, bias, C, ldc, M, N, K, epilogue, 0, 0, stream);
 }
 
 int tf_gemm_tiled(const void* A, int64_t lda, const void* W, int64_t ldw, const float* bias, void* C,
-                  int64_t ldc, int64_t M, int64_t N, int64_t K, int epilogue, int tile_n, void* stream) {
+                  int64_t ldc, int64_t M, int64_t N, int64_t K, int epilogue, int tile_n, int pair, void* stream) {
   int rc = begin_call();
   if (rc) return rc;
   if (tile_n != 0 && tile_n != 64 && tile_n != 128 && tile_n != 256)
     return set_error(TF_ERR_SHAPE, "tf_gemm_tiled: tile_n=%d (0, 64, 128 or 256)", tile_n);
   if (tile_n != 0 && N % tile_n != 0) return set_error(TF_ERR_SHAPE, "tf_gemm_tiled: N %% tile_n != 0");
-  return gemm_common(A, lda, W, ldw, bias, C, ldc, M, N, K, epilogue, tile_n, stream);
+  if (pair < 0 || pair > 2) return set_error(TF_ERR_SHAPE, "tf_gemm_tiled: pair=%d (0, 1 or 2)", pair);
+  if (pair == 2 && tile_n == 64) return set_error(TF_ERR_SHAPE, "tf_gemm_tiled: 2-SM tiles are 128 or 256 wide");
+  return gemm_common(A, lda, W, ldw, bias, C, ldc, M, N, K, epilogue, tile_n, pair, stream);
 }
 
 int tf_gemm_residual(const void* A, int64_t lda, const void* W, int64_t ldw, const float* bias,

@@ -78,8 +78,8 @@ struct AttnCfg {
   static constexpr int kPBytes = kAttnBM * kAttnBN * 2;
   static constexpr int kBarOff = kPOff + kAttnTiles * kPBytes;
   // q_full, k_full/empty[KS], v_full/empty[VS], s_full[2], s_free[2],
-  // p_full[2], o_full[2], drain
-  static constexpr int kNumBars = 1 + 2 * kKStages + 2 * kVStages + 8 + 1;
+  // p_full[2], o_full[2], turn[2], drain
+  static constexpr int kNumBars = 1 + 2 * kKStages + 2 * kVStages + 10 + 1;
   static constexpr int kBytes = kBarOff + kNumBars * 8 + 16;
   static constexpr int kAlloc = kBytes + 1024;
   // TMEM columns
@@ -173,7 +173,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint64_t* s_free = s_full + 2;
   uint64_t* p_full = s_free + 2;
   uint64_t* o_full = p_full + 2;
-  uint64_t* drain = o_full + 2;
+  uint64_t* turn = o_full + 2;  // exp-phase hand-off between the two softmax warpgroups
+  uint64_t* drain = turn + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
 
   const int warp = warp_id();
@@ -217,6 +218,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       mbar_init(&s_free[i], 128);
       mbar_init(&p_full[i], 128);
       mbar_init(&o_full[i], 1);
+      mbar_init(&turn[i], 128);
     }
     mbar_init(drain, 1);
     fence_mbar_init();
@@ -368,6 +370,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const uint8_t* kvalid = p.key_valid ? p.key_valid + static_cast<long long>(b) * p.seq_k : nullptr;
     uint8_t* prow = smem + C::kPOff + t * C::kPBytes + r * 128;
     const int nb = nblk[t];
+    const int n_pp = nblk[0] < nblk[1] ? nblk[0] : nblk[1];  // blocks where both tiles take turns
     const float c = p.scale_log2;
 
     float m_ref = -INFINITY;  // reference max (scaled log2 domain)
@@ -379,14 +382,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       tc_fence_after();
       float s[128];
       {
-        uint32_t v[32];
+        uint32_t v[128];
+        tmem_ld128(tm_s, v);  // the whole S row in one load, one wait
+        tmem_wait_ld();
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          tmem_ld32(tm_s + q * 32, v);
-          tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) s[q * 32 + i] = __uint_as_float(v[i]);
-        }
+        for (int i = 0; i < 128; ++i) s[i] = __uint_as_float(v[i]);
       }
       tc_fence_before();
       mbar_arrive(&s_free[t]);
@@ -455,7 +455,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
       const float m_use = m_ref == -INFINITY ? 0.f : m_ref;
 
-      // ---- probabilities -> fp16 pairs (and the row sum) ----
+      // ---- exp phase, in turns with the other tile's warpgroup ----
+      // tile 0 of block j goes after tile 1 of block j-1, tile 1 of block j
+      // after tile 0 of block j, so one group's exponentials overlap the
+      // other group's TMEM load / max / P store.
+      if (j < n_pp && (t == 1 || j > 0)) {
+        const uint32_t par = t == 0 ? ((j - 1) & 1) : (j & 1);
+        if (!(ok = mbar_wait(&turn[t], par, p.status, kDevTimeoutSoftmax))) break;
+      }
       uint32_t pk[64];
       float ls[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
@@ -475,6 +482,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         }
       }
       if constexpr (!C::kLFromMma) l += ((ls[0] + ls[1]) + (ls[2] + ls[3])) + ((ls[4] + ls[5]) + (ls[6] + ls[7]));
+      if (j < n_pp) mbar_arrive(&turn[1 - t]);
 
       // P buffer is free once PV of block j-1 has completed
       if (j > 0) {
@@ -501,20 +509,21 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           // fall through to the barrier; nothing is written
         } else {
           tc_fence_after();
-#pragma unroll
-          for (int q = 0; q < C::kNO / 32; ++q) {
-            uint32_t v[32];
-            tmem_ld32(tm_o + q * 32, v);
+          if constexpr (HD == 128) {
+            uint32_t v[128];
+            tmem_ld128(tm_o, v);
             tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) ov[q * 32 + i] = v[i];
-          }
-          if constexpr (C::kNO % 32 == 16) {
-            uint32_t v[16];
-            tmem_ld16(tm_o + (C::kNO / 32) * 32, v);
+            for (int i = 0; i < 128; ++i) ov[i] = v[i];
+          } else {
+            uint32_t v[64], w[16];
+            tmem_ld64(tm_o, v);
+            tmem_ld16(tm_o + 64, w);
             tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 16; ++i) ov[(C::kNO / 32) * 32 + i] = v[i];
+            for (int i = 0; i < 64; ++i) ov[i] = v[i];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) ov[64 + i] = w[i];
           }
           if constexpr (C::kLFromMma) l = __uint_as_float(ov[HD]);
         }

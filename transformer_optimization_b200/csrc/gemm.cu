@@ -33,6 +33,7 @@ namespace tfb {
 constexpr int kGemmBM = 128;
 constexpr int kGemmBK = 64;  // one 128-byte swizzle row of fp16
 constexpr int kGemmThreads = 192;
+constexpr int kEpiTileFloats = 32 * 33;  // one warp's epilogue staging tile
 
 struct GemmArgs {
   const float* bias;
@@ -54,11 +55,58 @@ struct GemmSmem {
   static constexpr int kABytes = kGemmBM * kGemmBK * 2;  // 16 KB
   static constexpr int kBBytes = BN * kGemmBK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kBarOffset = STAGES * kStageBytes;
+  static constexpr int kEpiOffset = STAGES * kStageBytes;  // 4 warps x 32x33 floats
+  static constexpr int kBarOffset = kEpiOffset + 4 * kEpiTileFloats * 4;
   // full[STAGES], empty[STAGES], tfull[2], tempty[2], drain, tmem slot
   static constexpr int kBytes = kBarOffset + (2 * STAGES + 5) * 8 + 16;
   static constexpr int kAlloc = kBytes + 1024;  // slack for 1024-byte alignment
 };
+
+// Epilogue of one 32-row x 32-column accumulator chunk, cooperatively by the
+// warp that read it from TMEM (lane i holds row row0+i). The chunk is staged
+// through a padded shared-memory tile (32 x 33 floats, conflict-free both
+// ways) so that the global accesses run along rows: lane L handles columns
+// 4*(L%8)..+3 of rows it*4 + L/8, i.e. each store instruction covers 4 rows
+// x 64 B (fp16) or 4 rows x 128 B (fp32) instead of 32 scattered rows.
+template <int EPI>
+__device__ __forceinline__ void epilogue_chunk(const GemmArgs& p, const uint32_t (&r)[32], float* buf, int row0,
+                                               int col0) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) buf[lane * 33 + i] = __uint_as_float(r[i]);
+  __syncwarp();
+  const int c4 = (lane & 7) * 4;
+  const float4 bq = __ldg(reinterpret_cast<const float4*>(p.bias + col0 + c4));
+#pragma unroll 2
+  for (int it = 0; it < 8; ++it) {
+    const int rl = it * 4 + (lane >> 3);
+    const int row = row0 + rl;
+    const float* src = buf + rl * 33 + c4;
+    float v0 = src[0] + bq.x, v1 = src[1] + bq.y, v2 = src[2] + bq.z, v3 = src[3] + bq.w;
+    if (row < p.M) {
+      if constexpr (EPI == 2) {
+        const long long off = static_cast<long long>(row) * p.ldx + col0 + c4;
+        const float4 xv = *reinterpret_cast<const float4*>(p.x_in + off);
+        bool valid = true;
+        if (p.mask_mode != 0) valid = p.valid[row] != 0;
+        if (p.mask_mode == 1 && !valid) v0 = v1 = v2 = v3 = 0.f;
+        float4 o = make_float4(xv.x + v0, xv.y + v1, xv.z + v2, xv.w + v3);
+        if (p.mask_mode == 2 && !valid) o = make_float4(0.f, 0.f, 0.f, 0.f);
+        *reinterpret_cast<float4*>(p.x_out + off) = o;
+      } else {
+        if constexpr (EPI == 1) {
+          v0 = v0 * 0.5f * (1.0f + erff(v0 * 0.7071067811865476f));
+          v1 = v1 * 0.5f * (1.0f + erff(v1 * 0.7071067811865476f));
+          v2 = v2 * 0.5f * (1.0f + erff(v2 * 0.7071067811865476f));
+          v3 = v3 * 0.5f * (1.0f + erff(v3 * 0.7071067811865476f));
+        }
+        *reinterpret_cast<uint2*>(p.C + static_cast<long long>(row) * p.ldc + col0 + c4) =
+            make_uint2(pack_half2(v0, v1), pack_half2(v2, v3));
+      }
+    }
+  }
+  __syncwarp();  // the tile is reused by the next chunk
+}
 
 template <int BN, int STAGES, int EPI>
 __global__ void __launch_bounds__(kGemmThreads, 1)
@@ -173,7 +221,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else {
     // ---------------- epilogue (warps 2..5) ----------------
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
-    const int row_in_tile = quarter * 32 + lane;
+    float* ebuf = reinterpret_cast<float*>(smem + L::kEpiOffset) + (warp - 2) * kEpiTileFloats;
     int tc = 0;
     for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++tc) {
       const int m0 = (t / p.n_tiles) * kGemmBM;
@@ -182,66 +230,24 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const uint32_t aph = (tc >> 1) & 1;
       if (!mbar_wait(&tfull[a], aph, p.status, kDevTimeoutEpilogue)) break;
       tc_fence_after();
-      const int row = m0 + row_in_tile;
-      const bool row_ok = row < p.M;
+      const int row0 = m0 + quarter * 32;
       const uint32_t t_addr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + a * BN;
-#pragma unroll 1
+      uint32_t r0[32], r1[32];
+      tmem_ld32(t_addr, r0);
+#pragma unroll
       for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(t_addr + c * 32, r);
         tmem_wait_ld();
-        if (c == BN / 32 - 1) {
+        uint32_t(&cur)[32] = (c & 1) ? r1 : r0;
+        uint32_t(&nxt)[32] = (c & 1) ? r0 : r1;
+        if (c + 1 < BN / 32) {
+          tmem_ld32(t_addr + (c + 1) * 32, nxt);
+        } else {
           // accumulator fully read: hand the buffer back to the MMA warp
           tc_fence_before();
           mbar_arrive(&tempty[a]);
         }
         const int col0 = n0 + c * 32;
-        if (!row_ok || col0 >= p.N) continue;
-        const float4* bsrc = reinterpret_cast<const float4*>(p.bias + col0);
-        float acc[32];
-#pragma unroll
-        for (int v = 0; v < 8; ++v) {
-          const float4 bq = __ldg(bsrc + v);
-          acc[4 * v + 0] = __uint_as_float(r[4 * v + 0]) + bq.x;
-          acc[4 * v + 1] = __uint_as_float(r[4 * v + 1]) + bq.y;
-          acc[4 * v + 2] = __uint_as_float(r[4 * v + 2]) + bq.z;
-          acc[4 * v + 3] = __uint_as_float(r[4 * v + 3]) + bq.w;
-        }
-        if constexpr (EPI == 2) {
-          const long long xoff = static_cast<long long>(row) * p.ldx + col0;
-          const float4* xi = reinterpret_cast<const float4*>(p.x_in + xoff);
-          float4* xo = reinterpret_cast<float4*>(p.x_out + xoff);
-          bool valid = true;
-          if (p.mask_mode != 0) valid = p.valid[row] != 0;
-          const float dscale = (p.mask_mode == 1 && !valid) ? 0.f : 1.f;
-          const bool zero = p.mask_mode == 2 && !valid;
-#pragma unroll
-          for (int v = 0; v < 8; ++v) {
-            const float4 xv = xi[v];
-            float4 o;
-            o.x = zero ? 0.f : xv.x + acc[4 * v + 0] * dscale;
-            o.y = zero ? 0.f : xv.y + acc[4 * v + 1] * dscale;
-            o.z = zero ? 0.f : xv.z + acc[4 * v + 2] * dscale;
-            o.w = zero ? 0.f : xv.w + acc[4 * v + 3] * dscale;
-            xo[v] = o;
-          }
-        } else {
-          uint32_t outw[16];
-#pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            float h0 = acc[2 * j], h1 = acc[2 * j + 1];
-            if constexpr (EPI == 1) {
-              h0 = h0 * 0.5f * (1.0f + erff(h0 * 0.7071067811865476f));
-              h1 = h1 * 0.5f * (1.0f + erff(h1 * 0.7071067811865476f));
-            }
-            outw[j] = pack_half2(h0, h1);
-          }
-          __half* crow = p.C + static_cast<long long>(row) * p.ldc + col0;
-          uint4* dst = reinterpret_cast<uint4*>(crow);
-#pragma unroll
-          for (int v = 0; v < 4; ++v)
-            dst[v] = make_uint4(outw[4 * v], outw[4 * v + 1], outw[4 * v + 2], outw[4 * v + 3]);
-        }
+        if (col0 < p.N && row0 < p.M) epilogue_chunk<EPI>(p, cur, ebuf, row0, col0);
       }
     }
   }
@@ -251,6 +257,191 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, 2 * BN);
+  }
+}
+
+
+// ---------------------------------------------------------------------------
+// 2-SM variant: a CTA pair (cluster of 2) computes a 256 x BN tile with
+// tcgen05.mma.cta_group::2. Each CTA loads its 128 rows of A and half of the
+// tile's BN rows of W, so per SM the operand traffic per flop drops by a
+// third against the 1-CTA 128 x BN tile and six stages fit in shared memory.
+// The leader CTA (rank 0) issues the MMAs; its commits arrive on the
+// barriers of both CTAs; both CTAs run the epilogue on their own 128 rows.
+//   warp 0      TMA producer (both CTAs, transaction bytes on the leader)
+//   warp 1      TMEM allocator (both), MMA issuer (leader)
+//   warps 2..9  epilogue: two warpgroups, each half of the BN columns
+// ---------------------------------------------------------------------------
+constexpr int kGemm2Threads = 320;
+
+template <int BN, int STAGES>
+struct Gemm2Smem {
+  static constexpr int kABytes = 128 * kGemmBK * 2;       // 16 KB: this CTA's A rows
+  static constexpr int kBBytes = (BN / 2) * kGemmBK * 2;  // this CTA's half of W
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kEpiOffset = STAGES * kStageBytes;  // 8 warps x 32x33 floats
+  static constexpr int kBarOffset = kEpiOffset + 8 * kEpiTileFloats * 4;
+  static constexpr int kBytes = kBarOffset + (2 * STAGES + 5) * 8 + 16;
+  static constexpr int kAlloc = kBytes + 1024;
+};
+
+template <int BN, int STAGES, int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemm2Threads, 1)
+    gemm_f16_tcgen05_2sm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                         GemmArgs p) {
+  using L = Gemm2Smem<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int cluster_id = blockIdx.x >> 1;
+  const int n_clusters = gridDim.x >> 1;
+  const int total_tiles = p.m_tiles * p.n_tiles;  // m_tiles counts 256-row tiles here
+  const int a_blocks = (p.K + kGemmBK - 1) / kGemmBK;
+  const int k_blocks = a_blocks * p.a_repeat;
+
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_map(&tmA);
+    tma_prefetch_map(&tmB);
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 16);  // one arrival per epilogue warp of both CTAs
+    }
+    mbar_init(drain, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, 2 * BN);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync_all();  // barriers of both CTAs initialised before any remote arrive
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer (both CTAs) ----------------
+      int it = 0;
+      bool ok = true;
+      for (int t = cluster_id; t < total_tiles && ok; t += n_clusters) {
+        const int m0 = (t / p.n_tiles) * 256 + static_cast<int>(rank) * 128;
+        const int n0 = (t % p.n_tiles) * BN + static_cast<int>(rank) * (BN / 2);
+        for (int kb = 0; kb < k_blocks; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!mbar_wait(&empty[s], ph ^ 1, p.status, kDevTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + s * L::kStageBytes;
+          const uint32_t bar = mapa_shared(smem_u32(&full[s]), 0);
+          if (leader) mbar_arrive_expect_tx(&full[s], 2 * L::kStageBytes);
+          const int akb = kb < a_blocks ? kb : kb - a_blocks;
+          const int wcol = kb < a_blocks ? kb * kGemmBK : p.K + akb * kGemmBK;
+          tma_load_2d_pair(sa, &tmA, bar, akb * kGemmBK, m0);
+          tma_load_2d_pair(sa + L::kABytes, &tmB, bar, wcol, n0);
+        }
+      }
+      // Drain: wait until the MMAs have consumed every stage this CTA loaded
+      // (the commit that frees a stage also proves its loads landed).
+      const int first = it > STAGES ? it - STAGES : 0;
+      for (int j = first; j < it; ++j)
+        mbar_wait(&empty[j % STAGES], ((j / STAGES) & 1), p.status, kDevTimeoutDrain);
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // ---------------- MMA issuer (leader) ----------------
+      constexpr uint32_t idesc = idesc_f16_f32(256, BN);
+      const uint32_t smem_base = smem_u32(smem);
+      int it = 0;
+      int tc = 0;
+      bool ok = true;
+      for (int t = cluster_id; t < total_tiles && ok; t += n_clusters, ++tc) {
+        const int a = tc & 1;
+        const uint32_t aph = (tc >> 1) & 1;
+        if (!mbar_wait(&tempty[a], aph ^ 1, p.status, kDevTimeoutMma)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + a * BN;
+        for (int kb = 0; kb < k_blocks; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!mbar_wait(&full[s], ph, p.status, kDevTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_base + s * L::kStageBytes;
+          const uint32_t sb = sa + L::kABytes;
+#pragma unroll
+          for (int k = 0; k < kGemmBK / 16; ++k)
+            umma_f16_ss_pair(d_tmem, smem_desc_sw128(sa + k * 32, 16, 1024), smem_desc_sw128(sb + k * 32, 16, 1024),
+                             idesc, (kb | k) != 0 ? 1u : 0u);
+          umma_commit_pair_mc(&empty[s], 0x3);
+        }
+        if (ok) umma_commit_pair_mc(&tfull[a], 0x3);
+      }
+      umma_commit_pair_mc(drain, 0x1);
+      mbar_wait(drain, 0, p.status, kDevTimeoutDrain);
+    }
+  } else {
+    // ---------------- epilogue (warps 2..9, both CTAs) ----------------
+    const int ew = warp - 2;
+    const int half = ew >> 2;       // which half of the BN columns
+    const int quarter = warp & 3;   // TMEM lane quarter this warp may access
+    float* ebuf = reinterpret_cast<float*>(smem + L::kEpiOffset) + ew * kEpiTileFloats;
+    const uint32_t tempty_leader = mapa_shared(smem_u32(&tempty[0]), 0);
+    int tc = 0;
+    for (int t = cluster_id; t < total_tiles; t += n_clusters, ++tc) {
+      const int m0 = (t / p.n_tiles) * 256 + static_cast<int>(rank) * 128;
+      const int n0 = (t % p.n_tiles) * BN + half * (BN / 2);
+      const int a = tc & 1;
+      const uint32_t aph = (tc >> 1) & 1;
+      if (!mbar_wait(&tfull[a], aph, p.status, kDevTimeoutEpilogue)) break;
+      tc_fence_after();
+      const int row0 = m0 + quarter * 32;
+      const uint32_t t_addr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + a * BN + half * (BN / 2);
+      constexpr int NCH = BN / 64;  // 32-column chunks per half
+      uint32_t r0[32], r1[32];
+      tmem_ld32(t_addr, r0);
+#pragma unroll
+      for (int c = 0; c < NCH; ++c) {
+        tmem_wait_ld();
+        uint32_t(&cur)[32] = (c & 1) ? r1 : r0;
+        uint32_t(&nxt)[32] = (c & 1) ? r0 : r1;
+        if (c + 1 < NCH) {
+          tmem_ld32(t_addr + (c + 1) * 32, nxt);
+        } else {
+          // accumulator fully read: hand the buffer back to the leader's MMA
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(tempty_leader + a * 8);
+        }
+        const int col0 = n0 + c * 32;
+        if (col0 < p.N && row0 < p.M) epilogue_chunk<EPI>(p, cur, ebuf, row0, col0);
+      }
+    }
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  cluster_sync_all();  // neither CTA leaves while its pair may still touch it
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, 2 * BN);
   }
 }
 
@@ -274,6 +465,25 @@ static int launch_gemm_cfg(const CUtensorMap& ta, const CUtensorMap& tb, const G
   kern<<<grid, kGemmThreads, L::kAlloc, stream>>>(ta, tb, args);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(TF_ERR_LAUNCH, "gemm launch: %s", cudaGetErrorString(e));
+  return TF_OK;
+}
+
+template <int BN, int STAGES, int EPI>
+static int launch_gemm2_cfg(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args, int grid,
+                            cudaStream_t stream) {
+  using L = Gemm2Smem<BN, STAGES>;
+  auto kern = gemm_f16_tcgen05_2sm<BN, STAGES, EPI>;
+  static bool attr_done[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_done[dev & 63]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
+    if (e != cudaSuccess) return set_error(TF_ERR_LAUNCH, "cudaFuncSetAttribute(gemm2): %s", cudaGetErrorString(e));
+    attr_done[dev & 63] = true;
+  }
+  kern<<<grid, kGemm2Threads, L::kAlloc, stream>>>(ta, tb, args);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_error(TF_ERR_LAUNCH, "gemm2 launch: %s", cudaGetErrorString(e));
   return TF_OK;
 }
 
@@ -324,11 +534,32 @@ int gemm_f16(const GemmCall& g, cudaStream_t stream) {
   const int m_tiles = static_cast<int>((M + kGemmBM - 1) / kGemmBM);
   int bn = g.tile_n > 0 ? g.tile_n : choose_bn(m_tiles, static_cast<int>(N), sms);
   if (N % bn != 0) bn = (N % 128 == 0) ? 128 : 64;
+  // 2-SM pairs for grids that fill the device; 1-CTA tiles (more of them)
+  // for small problems
+  bool pair = false;
+  if (g.pair == 2) {
+    pair = true;
+  } else if (g.pair == 0) {
+    const long long pair_tiles = ((M + 255) / 256) * (N / (N % 256 == 0 ? 256 : 128));
+    pair = (N % 128 == 0) && pair_tiles >= sms / 2;
+  }
+  if (pair) {
+    if (N % 128 != 0) return set_error(TF_ERR_SHAPE, "gemm: 2-SM tiles need N %% 128 == 0");
+    bn = (g.tile_n == 128 || N % 256 != 0) ? 128 : 256;
+    if (g.tile_n == 0 && bn == 256) {
+      // wave quantisation: prefer 128-wide pair tiles when they fill the
+      // device in fewer weighted waves
+      const long long mt = (M + 255) / 256;
+      const long long c256 = mt * (N / 256), c128 = mt * (N / 128);
+      const int nc = sms / 2;
+      if (1.1 * double((c128 + nc - 1) / nc) < 2.0 * double((c256 + nc - 1) / nc)) bn = 128;
+    }
+  }
 
   CUtensorMap ta, tb;
-  int rc = make_tmap_2d_f16(&ta, g.A, K, M, g.lda, kGemmBK, kGemmBM);
+  int rc = make_tmap_2d_f16(&ta, g.A, K, M, g.lda, kGemmBK, 128);
   if (rc) return rc;
-  rc = make_tmap_2d_f16(&tb, g.W, K * g.a_repeat, N, g.ldw, kGemmBK, bn);
+  rc = make_tmap_2d_f16(&tb, g.W, K * g.a_repeat, N, g.ldw, kGemmBK, pair ? bn / 2 : bn);
   if (rc) return rc;
 
   GemmArgs args;
@@ -344,11 +575,24 @@ int gemm_f16(const GemmCall& g, cudaStream_t stream) {
   args.N = static_cast<int>(N);
   args.K = static_cast<int>(K);
   args.a_repeat = g.a_repeat;
-  args.m_tiles = m_tiles;
+  args.m_tiles = pair ? static_cast<int>((M + 255) / 256) : m_tiles;
   args.n_tiles = static_cast<int>((N + bn - 1) / bn);
   args.status = device_status_ptr();
   if (args.status == nullptr) return last_error_code();
   const long long tiles = static_cast<long long>(args.m_tiles) * args.n_tiles;
+  if (pair) {
+    const int max_clusters = sms / 2;
+    const int clusters = static_cast<int>(tiles < max_clusters ? tiles : max_clusters);
+    const int grid2 = 2 * clusters;
+    switch ((bn == 256 ? 0 : 3) + g.epilogue) {
+      case 0: return launch_gemm2_cfg<256, 6, 0>(ta, tb, args, grid2, stream);
+      case 1: return launch_gemm2_cfg<256, 6, 1>(ta, tb, args, grid2, stream);
+      case 2: return launch_gemm2_cfg<256, 6, 2>(ta, tb, args, grid2, stream);
+      case 3: return launch_gemm2_cfg<128, 8, 0>(ta, tb, args, grid2, stream);
+      case 4: return launch_gemm2_cfg<128, 8, 1>(ta, tb, args, grid2, stream);
+      default: return launch_gemm2_cfg<128, 8, 2>(ta, tb, args, grid2, stream);
+    }
+  }
   const int grid = static_cast<int>(tiles < sms ? tiles : sms);
 
 #define TFB_GEMM_EPI(BN, ST)                                                         \

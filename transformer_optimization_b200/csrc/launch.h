@@ -51,6 +51,7 @@ struct GemmCall {
   int epilogue;
   int a_repeat;
   int tile_n;
+  int pair;  // 0 automatic, 1 one-CTA tiles, 2 two-SM (CTA pair) tiles
 };
 
 int gemm_f16(const GemmCall& g, cudaStream_t stream);

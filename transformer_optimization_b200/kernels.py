@@ -99,7 +99,8 @@ def split_weight(w: torch.Tensor) -> torch.Tensor:
 
 
 def linear(a: torch.Tensor, w: torch.Tensor, b: torch.Tensor, *, gelu: bool = False,
-           out: Optional[torch.Tensor] = None, tile_n: int = 0, w_split: bool = False) -> torch.Tensor:
+           out: Optional[torch.Tensor] = None, tile_n: int = 0, w_split: bool = False,
+           pair: int = 0) -> torch.Tensor:
     """fp16 GEMM on tcgen05 (tf_gemm): out = fp16([gelu](a @ w.T + b)), a
     [..., K] fp16 with unit inner stride, w [N, K] fp16 (or split_weight's
     [N, 2K] with w_split), b [N] fp32."""
@@ -112,9 +113,9 @@ def linear(a: torch.Tensor, w: torch.Tensor, b: torch.Tensor, *, gelu: bool = Fa
     if o2.stride(-1) != 1 or o2.dtype != torch.float16:
         raise ValueError("linear: out must be fp16 with a unit inner stride")
     epi = (_abi.TF_EPI_BIAS_GELU if gelu else _abi.TF_EPI_BIAS) | (_abi.TF_EPI_W_SPLIT if w_split else 0)
-    if tile_n:
+    if tile_n or pair:
         _abi.call("tf_gemm_tiled", _ptr(a2), a2.stride(0), _ptr(w), w.stride(0), _ptr(b), _ptr(o2), o2.stride(0),
-                  m, n, k, epi, tile_n, _stream())
+                  m, n, k, epi, tile_n, pair, _stream())
     else:
         _abi.call("tf_gemm", _ptr(a2), a2.stride(0), _ptr(w), w.stride(0), _ptr(b), _ptr(o2), o2.stride(0),
                   m, n, k, epi, _stream())

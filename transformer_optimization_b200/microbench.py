@@ -21,18 +21,34 @@ import torch
 from . import kernels as K
 
 
-def _time(fn, warmup, iters):
-    for _ in range(warmup):
+def _time(fn, warmup, iters, min_warm_s=0.3, min_time_s=0.2):
+    """Mean ms per launch. Warm-up runs at least `warmup` launches and
+    `min_warm_s` seconds (so clocks have ramped); the timed loop runs at
+    least `iters` launches and `min_time_s` seconds."""
+    import time
+    t0 = time.perf_counter()
+    n = 0
+    while n < warmup or (min_warm_s > 0 and time.perf_counter() - t0 < min_warm_s):
         fn()
+        n += 1
+        if n % 16 == 0:
+            torch.cuda.synchronize()
     torch.cuda.synchronize()
+    # size the timed loop from one measured launch
     s = torch.cuda.Event(enable_timing=True)
     e = torch.cuda.Event(enable_timing=True)
     s.record()
-    for _ in range(iters):
+    fn()
+    e.record()
+    torch.cuda.synchronize()
+    one = max(s.elapsed_time(e), 1e-3)
+    reps = max(iters, int(min_time_s * 1e3 / one))
+    s.record()
+    for _ in range(reps):
         fn()
     e.record()
     torch.cuda.synchronize()
-    return s.elapsed_time(e) / iters
+    return s.elapsed_time(e) / reps
 
 
 def main(argv=None):
@@ -41,28 +57,34 @@ def main(argv=None):
     ap.add_argument("dims", type=int, nargs="+")
     ap.add_argument("--gelu", action="store_true")
     ap.add_argument("--causal", action="store_true")
+    ap.add_argument("--exp-f32", action="store_true", help="flash: fp32 exp2 path")
     ap.add_argument("--tile-n", type=int, default=0)
+    ap.add_argument("--pair", type=int, default=0, help="0 auto, 1 one-CTA tiles, 2 two-SM tiles")
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--iters", type=int, default=10)
+    ap.add_argument("--min-warm-s", type=float, default=0.3, help="minimum warm-up seconds (0 for ncu)")
+    ap.add_argument("--min-time-s", type=float, default=0.2, help="minimum timed seconds (0 for ncu)")
     a = ap.parse_args(argv)
+    T = lambda fn: _time(fn, a.warmup, a.iters, a.min_warm_s, a.min_time_s)
     torch.manual_seed(0)
     dev = torch.device("cuda")
     if a.kernel == "gemm":
         m, n, k = a.dims
         x = torch.randn(m, k, device=dev).half()
         w = (torch.randn(n, k, device=dev) / math.sqrt(k)).half()
-        b = torch.randn(n, device=dev).half()
+        b = torch.randn(n, device=dev)
         out = torch.empty(m, n, device=dev, dtype=torch.float16)
-        ms = _time(lambda: K.linear(x, w, b, gelu=a.gelu, out=out, tile_n=a.tile_n), a.warmup, a.iters)
+        ms = T(lambda: K.linear(x, w, b, gelu=a.gelu, out=out, tile_n=a.tile_n, pair=a.pair))
         rate = 2.0 * m * n * k / (ms / 1e3) / 1e12
-        print(f"gemm M={m} N={n} K={k} gelu={a.gelu} tile_n={a.tile_n}: {ms:.4f} ms  {rate:.1f} TFLOP/s")
+        print(f"gemm M={m} N={n} K={k} gelu={a.gelu} tile_n={a.tile_n} pair={a.pair}: {ms:.4f} ms  "
+              f"{rate:.1f} TFLOP/s")
     elif a.kernel == "flash":
         bsz, h, s, hd = a.dims
         d = h * hd
         qkv = torch.randn(bsz, s, 3 * d, device=dev).half()
         out = torch.empty(bsz, s, d, device=dev, dtype=torch.float16)
-        ms = _time(lambda: K.flash_attention(qkv[..., :d], qkv[..., d:2 * d], qkv[..., 2 * d:], h, hd ** -0.5,
-                                             causal=a.causal, out=out), a.warmup, a.iters)
+        ms = T(lambda: K.flash_attention(qkv[..., :d], qkv[..., d:2 * d], qkv[..., 2 * d:], h, hd ** -0.5,
+                                         causal=a.causal, out=out, exp_f32=a.exp_f32))
         flops = 4.0 * bsz * s * s * d * (0.5 if a.causal else 1.0)
         print(f"flash B={bsz} H={h} S={s} hd={hd} causal={a.causal}: {ms:.4f} ms  "
               f"{flops / (ms / 1e3) / 1e12:.1f} TFLOP/s")
@@ -74,8 +96,7 @@ def main(argv=None):
         b = torch.zeros(d, device=dev)
         xo = torch.empty_like(x)
         nrm = torch.empty(m, d, device=dev, dtype=torch.float16)
-        ms = _time(lambda: K.ln_residual(x, delta, w, b, 1e-5, write_x=True, x_out=xo, normed=nrm),
-                   a.warmup, a.iters)
+        ms = T(lambda: K.ln_residual(x, delta, w, b, 1e-5, write_x=True, x_out=xo, normed=nrm))
         print(f"ln M={m} D={d}: {ms:.4f} ms  {m * d * 12 / (ms / 1e3) / 1e9:.1f} GB/s")
 
 
