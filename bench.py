@@ -145,7 +145,7 @@ def kernel_profile(model, x):
     Returns {kernel: (launches, total_ms, algorithmic units)}."""
     cfg = model.config
     rec = {"gemm": [], "flash": [], "ln": []}
-    orig = (K.linear, K.flash_attention, K.ln_residual)
+    orig = (K.linear, K.flash_attention, K.ln_residual, K.linear_residual)
 
     def wrap(name, f, units):
         def g(*a, **kw):
@@ -158,7 +158,9 @@ def kernel_profile(model, x):
             return r
         return g
 
-    def gemm_flops(a, w, b, **kw):
+    def gemm_flops(a, w, b, *args, **kw):
+        # algorithmic flops of the projection (split weights do twice the
+        # tensor work for the same product; counted once)
         return 2.0 * (a.numel() // a.shape[-1]) * a.shape[-1] * w.shape[0]
 
     def flash_flops(q, k, v, heads, scale, **kw):
@@ -176,13 +178,14 @@ def kernel_profile(model, x):
     K.linear = wrap("gemm", orig[0], gemm_flops)
     K.flash_attention = wrap("flash", orig[1], flash_flops)
     K.ln_residual = wrap("ln", orig[2], ln_bytes)
+    K.linear_residual = wrap("gemm", orig[3], gemm_flops)
     try:
         model.use_cuda_graphs = False
         with torch.inference_mode():
             model(x)
         torch.cuda.synchronize()
     finally:
-        K.linear, K.flash_attention, K.ln_residual = orig
+        K.linear, K.flash_attention, K.ln_residual, K.linear_residual = orig
         model.use_cuda_graphs = True
     out = {}
     for name, lst in rec.items():
@@ -320,7 +323,7 @@ def run_ours(args, cfg, rank, world, local_rank):
     gemm_tflops = fl_g / (ms_g / 1e3) / 1e12
     flash_tflops = fl_f / (ms_f / 1e3) / 1e12
     ln_gbs = by_l / (ms_l / 1e3) / 1e9
-    launches_per_step = 7 * cfg.num_layers + 1
+    launches_per_step = n_g + n_f + n_l
 
     line = {
         "metric": f"forward tokens/s ({args.config})", "value": value, "unit": "tokens/s", "n_gpus": world,
@@ -370,6 +373,76 @@ def run_ours(args, cfg, rank, world, local_rank):
         print(json.dumps(line), flush=True)
 
 
+def run_cp(args, cfg, rank, world, local_rank):
+    """Context-parallel forward of one long sequence over `world` GPUs (ring
+    attention over NCCL P2P). Strong scaling: the same sequence is split."""
+    import torch.distributed as dist
+
+    from transformer_optimization_b200.context_parallel import ContextParallelTransformer, shard_bounds
+    device = torch.device("cuda", local_rank)
+    peaks, peak_src = load_peaks()
+    flush_buf = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+    model = build_model(cfg, device)  # same seed on every rank: identical weights
+    bounds = shard_bounds(cfg.seq_len, world)
+    st, n = bounds[rank]
+    x_local = torch.randn(cfg.batch_size, n, cfg.d_model, device=device)
+    cp = ContextParallelTransformer(model)
+    with torch.inference_mode():
+        for _ in range(max(args.warmup, 3)):
+            cp.forward(x_local, bounds=bounds)
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+    smi_id = vis.split(",")[local_rank].strip() if vis else str(local_rank)
+    with ClockSampler(smi_id) as clk:
+        with torch.inference_mode():
+            ts = time_steps(lambda: cp.forward(x_local, bounds=bounds), args.steps, flush_buf)
+    torch.cuda.synchronize()
+    dist.barrier()
+    t = torch.tensor([sum(ts)], device=device, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_per_step = float(t.item()) / args.steps
+    tokens = cfg.batch_size * cfg.seq_len
+    value = tokens / (ms_per_step / 1e3)
+
+    x_host = torch.randn(cfg.batch_size, n, cfg.d_model).pin_memory()
+    y_host = torch.empty_like(x_host).pin_memory()
+
+    def e2e_step():
+        y = cp.forward(x_host.to(device, non_blocking=True), bounds=bounds)
+        y_host.copy_(y, non_blocking=True)
+
+    with torch.inference_mode():
+        e2e_step()
+        torch.cuda.synchronize()
+        dist.barrier()
+        e_ts = time_steps(e2e_step, args.steps, flush_buf)
+    t = torch.tensor([sum(e_ts)], device=device, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e_ms = float(t.item()) / args.steps
+    dist.barrier()
+    flops = count_dense_flops(cfg)
+    launches = cfg.num_layers * (6 + world + (world - 1)) + 1
+    line = {
+        "metric": f"forward tokens/s ({args.config})", "value": value, "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+        "config": {"workload": args.config, **cfg_dict(cfg), "global_batch": cfg.batch_size,
+                   "parallelism": f"cp{world}", "shard_tokens": n, "l2": "flushed between steps (256 MB write)",
+                   "weights": "default init, seed 0", "cuda_graph": False},
+        "mfu": flops / (ms_per_step / 1e3) / (peaks["bf16_tflops"] * 1e12 * world),
+        "latency_ms": ms_per_step,
+        "e2e": {"value": tokens / (e_ms / 1e3), "unit": "tokens/s",
+                "h2d_bytes_per_step": x_host.numel() * 4 * world, "d2h_bytes_per_step": y_host.numel() * 4 * world,
+                "ms_per_step": e_ms},
+        "gpu_launches": launches * args.steps,
+        "clocks": clk.summary(),
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[1])
     ap.add_argument("--gpus", type=int, default=1)
@@ -400,7 +473,10 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        run_ours(args, cfg, rank, world, local_rank)
+        if world > 1 and cfg.batch_size == 1:
+            run_cp(args, cfg, rank, world, local_rank)  # one sequence: context parallel
+        else:
+            run_ours(args, cfg, rank, world, local_rank)
     finally:
         if world > 1:
             import torch.distributed as dist

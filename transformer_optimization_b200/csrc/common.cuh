@@ -105,7 +105,8 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* s
 }
 
 // ---------------------------------------------------------------------------
-// TMA (cp.async.bulk.tensor), no multicast anywhere in this library
+// TMA tile loads (cp.async.bulk.tensor): plain loads only, each CTA fetches
+// its own tiles; remote data never feeds a TMA load
 // ---------------------------------------------------------------------------
 
 __device__ __forceinline__ void tma_prefetch_map(const CUtensorMap* map) {
@@ -282,7 +283,7 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
 
 // TMA tile load for a 2-SM MMA pair: lands in this CTA's shared memory and
 // signals the transaction bytes on `bar_cluster_addr`, which may be the
-// barrier of the pair's leader CTA. No multicast.
+// barrier of the pair's leader CTA. A plain (single-destination) load.
 __device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t bar_cluster_addr, int x,
                                                  int y) {
   asm volatile(

@@ -9,7 +9,8 @@
 // the two-pass moments over the row held in registers, as the reference
 // kernel does (mean first, then the centred sum of squares).
 //
-// Layout: one warp per row, 8 rows per 256-thread block. Each lane owns
+// Layout: one warp per row (grid-stride over rows), 8 warps per 256-thread
+// block, as many blocks as are resident on the device. Each lane owns
 // 8-element chunks (two float4 of x, one 16-byte vector of fp16 delta) at
 // chunk index lane + 32*i, so every warp-wide load is a contiguous,
 // fully-coalesced 512 B (fp32) or 256 B (fp16) segment. HBM-bound: bytes per
@@ -30,8 +31,9 @@ __global__ void __launch_bounds__(256) ln_residual_kernel(const float* __restric
                                                           int flags, float* __restrict__ x_out,
                                                           void* __restrict__ normed) {
   const int lane = threadIdx.x & 31;
-  const long long row = static_cast<long long>(blockIdx.x) * kLnRowsPerBlock + (threadIdx.x >> 5);
-  if (row >= M) return;
+  const long long warps_total = static_cast<long long>(gridDim.x) * kLnRowsPerBlock;
+  for (long long row = static_cast<long long>(blockIdx.x) * kLnRowsPerBlock + (threadIdx.x >> 5); row < M;
+       row += warps_total) {
   const int nchunk = D >> 3;
   const float* xr = x + row * D;
   bool row_valid = true;
@@ -118,6 +120,7 @@ __global__ void __launch_bounds__(256) ln_residual_kernel(const float* __restric
       }
     }
   }
+  }  // row loop
 }
 
 int ln_residual(const float* x, const void* delta, const float* w, const float* b, float eps,
@@ -135,13 +138,20 @@ int ln_residual(const float* x, const void* delta, const float* w, const float* 
   if ((flags & (TF_LN_MASK_DELTA | TF_LN_MASK_X | TF_LN_MASK_OUT)) && valid == nullptr)
     return set_error(TF_ERR_SHAPE, "ln_residual: mask flag without a valid-token mask");
   if (!(flags & (TF_LN_MASK_DELTA | TF_LN_MASK_X | TF_LN_MASK_OUT))) valid = nullptr;
-  const long long blocks = (M + kLnRowsPerBlock - 1) / kLnRowsPerBlock;
-  if (blocks > 0x7fffffffll) return set_error(TF_ERR_SHAPE, "ln_residual: M too large");
+  // grid-stride over rows with the device filled exactly (resident blocks
+  // per SM from the occupancy of this instantiation)
   const int nch = (D / 8 + 31) / 32;
   const __half* dh = static_cast<const __half*>(delta);
-  dim3 grid(static_cast<unsigned>(blocks));
-#define TFB_LN_CASE(N)                                                                                     \
-  ln_residual_kernel<N><<<grid, 256, 0, stream>>>(x, dh, w, b, eps, valid, M, D, flags, x_out, normed); \
+  const long long need = (M + kLnRowsPerBlock - 1) / kLnRowsPerBlock;
+#define TFB_LN_CASE(N)                                                                                        \
+  {                                                                                                           \
+    int per_sm = 1;                                                                                           \
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, ln_residual_kernel<N>, 256, 0);                    \
+    long long blocks = static_cast<long long>(device_sm_count()) * (per_sm > 0 ? per_sm : 1);                 \
+    if (blocks > need) blocks = need;                                                                         \
+    ln_residual_kernel<N><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(x, dh, w, b, eps, valid, M, D,   \
+                                                                             flags, x_out, normed);           \
+  }                                                                                                           \
   break;
   switch (nch <= 1 ? 1 : nch <= 2 ? 2 : nch <= 4 ? 4 : nch <= 8 ? 8 : 16) {
     case 1: TFB_LN_CASE(1)
