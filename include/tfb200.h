@@ -108,12 +108,13 @@ int tf_gemm_tiled(const void* A, int64_t lda, const void* W, int64_t ldw, const 
  *   x_out[M, N] = mask_x(x_in + mask_delta(A * W^T + bias))
  * x_in / x_out fp32 with pitch ldx (x_out may equal x_in: in place); valid
  * uint8 [M] for the mask modes. w_split != 0: W is [N, 2K] = [W_hi | W_lo].
+ * tile_n / pair: tiling as in tf_gemm_tiled (0, 0 = automatic).
  * Replaces out_proj / ffn_out (torch_transformer_benchmark.py:4163-4169,
  * 4194) together with the residual add of the following _ln_site
  * (torch_transformer_benchmark.py:3988-3995). */
 int tf_gemm_residual(const void* A, int64_t lda, const void* W, int64_t ldw, const float* bias,
                      const float* x_in, float* x_out, int64_t ldx, const uint8_t* valid, int mask_mode,
-                     int64_t M, int64_t N, int64_t K, int w_split, void* stream);
+                     int64_t M, int64_t N, int64_t K, int w_split, int tile_n, int pair, void* stream);
 
 /* Flash attention forward (online softmax, no score matrix in HBM):
  *   out[b, i, h*hd:(h+1)*hd] = sum_j softmax_j(scale * q_i . k_j) v_j

@@ -156,7 +156,7 @@ static inline int begin_call() {
 
 extern "C" {
 
-int tf_abi_version(void) { return 3; }
+int tf_abi_version(void) { return 4; }
 
 const char* tf_last_error(void) { return tfb::g_msg; }
 
@@ -230,9 +230,13 @@ int tf_gemm_tiled(const void* A, int64_t lda, const void* W, int64_t ldw, const 
 
 int tf_gemm_residual(const void* A, int64_t lda, const void* W, int64_t ldw, const float* bias,
                      const float* x_in, float* x_out, int64_t ldx, const uint8_t* valid, int mask_mode,
-                     int64_t M, int64_t N, int64_t K, int w_split, void* stream) {
+                     int64_t M, int64_t N, int64_t K, int w_split, int tile_n, int pair, void* stream) {
   int rc = begin_call();
   if (rc) return rc;
+  if (tile_n != 0 && tile_n != 64 && tile_n != 128 && tile_n != 256)
+    return set_error(TF_ERR_SHAPE, "tf_gemm_residual: tile_n=%d (0, 64, 128 or 256)", tile_n);
+  if (pair < 0 || pair > 2 || (pair == 2 && tile_n == 64))
+    return set_error(TF_ERR_SHAPE, "tf_gemm_residual: pair=%d with tile_n=%d", pair, tile_n);
   tfb::GemmCall g = {};
   g.A = A;
   g.lda = lda;
@@ -249,6 +253,8 @@ int tf_gemm_residual(const void* A, int64_t lda, const void* W, int64_t ldw, con
   g.K = K;
   g.epilogue = 2;
   g.a_repeat = w_split ? 2 : 1;
+  g.tile_n = tile_n;
+  g.pair = pair;
   return tfb::gemm_f16(g, as_stream(stream));
 }
 

@@ -102,6 +102,18 @@ __device__ __forceinline__ uint32_t ex2_pair_f16(float a, float b) {
   return r;
 }
 
+__device__ __forceinline__ float fmax3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+__device__ __forceinline__ uint32_t ex2_f16x2(uint32_t h) {
+  uint32_t r;
+  asm("ex2.approx.f16x2 %0, %1;" : "=r"(r) : "r"(h));
+  return r;
+}
+
 __device__ __forceinline__ uint32_t pack_f16x2_rn(float a, float b) {
   uint32_t h;
   asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(b), "f"(a));
@@ -428,16 +440,20 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         }
       }
 
-      // ---- row max (tree) ----
-      float mx[16];
+      // ---- row max: eight 3-input-max chains, then a short tree ----
+      // chain k covers s[k + 8*i] for i = 0..15 (all 128 columns)
+      float mx[8];
 #pragma unroll
-      for (int i = 0; i < 16; ++i) mx[i] = fmaxf(fmaxf(s[i], s[i + 16]), fmaxf(s[i + 32], s[i + 48]));
+      for (int k = 0; k < 8; ++k) mx[k] = fmax3f(s[k], s[8 + k], s[16 + k]);
 #pragma unroll
-      for (int i = 0; i < 16; ++i) mx[i] = fmaxf(mx[i], fmaxf(fmaxf(s[i + 64], s[i + 80]), fmaxf(s[i + 96], s[i + 112])));
+      for (int base = 24; base < 120; base += 16)
 #pragma unroll
-      for (int w = 8; w > 0; w >>= 1)
+        for (int k = 0; k < 8; ++k) mx[k] = fmax3f(mx[k], s[base + k], s[base + 8 + k]);
 #pragma unroll
-        for (int i = 0; i < w; ++i) mx[i] = fmaxf(mx[i], mx[i + w]);
+      for (int k = 0; k < 8; ++k) mx[k] = fmaxf(mx[k], s[120 + k]);
+      mx[0] = fmax3f(mx[0], mx[1], mx[2]);
+      mx[3] = fmax3f(mx[3], mx[4], mx[5]);
+      mx[0] = fmax3f(mx[0], mx[3], fmaxf(mx[6], mx[7]));
       const float m_row = mx[0] * c;
 
       // ---- lazy rescale of O (and l) ----
@@ -463,22 +479,31 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const uint32_t par = t == 0 ? ((j - 1) & 1) : (j & 1);
         if (!(ok = mbar_wait(&turn[t], par, p.status, kDevTimeoutSoftmax))) break;
       }
+      // three independent sweeps (scale, pack, exponentiate) so the exp
+      // unit streams back to back instead of waiting on each pair's chain
       uint32_t pk[64];
       float ls[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        const float a0 = fmaf(s[2 * i], c, -m_use);
-        const float a1 = fmaf(s[2 * i + 1], c, -m_use);
-        if constexpr (EXP16) {
-          pk[i] = ex2_pair_f16(a0, a1);
-          if constexpr (!C::kLFromMma) {
+      for (int i = 0; i < 128; ++i) s[i] = fmaf(s[i], c, -m_use);
+      if constexpr (EXP16) {
+#pragma unroll
+        for (int i = 0; i < 64; ++i) pk[i] = pack_f16x2_rn(s[2 * i], s[2 * i + 1]);
+#pragma unroll
+        for (int i = 0; i < 64; ++i) pk[i] = ex2_f16x2(pk[i]);
+        if constexpr (!C::kLFromMma) {
+#pragma unroll
+          for (int i = 0; i < 64; ++i) {
             const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&pk[i]));
             ls[i & 7] += f.x + f.y;
           }
-        } else {
-          const float e0 = ex2_f32(a0), e1 = ex2_f32(a1);
-          pk[i] = pack_f16x2_rn(e0, e1);
-          if constexpr (!C::kLFromMma) ls[i & 7] += e0 + e1;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 128; ++i) s[i] = ex2_f32(s[i]);
+#pragma unroll
+        for (int i = 0; i < 64; ++i) {
+          pk[i] = pack_f16x2_rn(s[2 * i], s[2 * i + 1]);
+          if constexpr (!C::kLFromMma) ls[i & 7] += s[2 * i] + s[2 * i + 1];
         }
       }
       if constexpr (!C::kLFromMma) l += ((ls[0] + ls[1]) + (ls[2] + ls[3])) + ((ls[4] + ls[5]) + (ls[6] + ls[7]));

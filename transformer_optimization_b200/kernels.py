@@ -124,7 +124,8 @@ def linear(a: torch.Tensor, w: torch.Tensor, b: torch.Tensor, *, gelu: bool = Fa
 
 def linear_residual(a: torch.Tensor, w: torch.Tensor, b: torch.Tensor, x_in: torch.Tensor,
                     x_out: Optional[torch.Tensor] = None, valid: Optional[torch.Tensor] = None, *,
-                    mask_delta: bool = False, mask_x: bool = False, w_split: bool = False) -> torch.Tensor:
+                    mask_delta: bool = False, mask_x: bool = False, w_split: bool = False, tile_n: int = 0,
+                    pair: int = 0) -> torch.Tensor:
     """GEMM closing a residual connection in fp32 (tf_gemm_residual):
     x_out = mask_x(x_in + mask_delta(a @ w.T + b)). x_in/x_out fp32 [..., N]
     contiguous (x_out may be x_in); valid bool/uint8 [rows] for the masks."""
@@ -147,7 +148,7 @@ def linear_residual(a: torch.Tensor, w: torch.Tensor, b: torch.Tensor, x_in: tor
     if valid is not None and not valid.is_contiguous():
         valid = valid.contiguous()
     _abi.call("tf_gemm_residual", _ptr(a2), a2.stride(0), _ptr(w), w.stride(0), _ptr(b), _ptr(x_in), _ptr(x_out), n,
-              _ptr(valid) if mode else None, mode, m, n, k, 1 if w_split else 0, _stream())
+              _ptr(valid) if mode else None, mode, m, n, k, 1 if w_split else 0, tile_n, pair, _stream())
     return x_out
 
 

@@ -53,7 +53,7 @@ def _time(fn, warmup, iters, min_warm_s=0.3, min_time_s=0.2):
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("kernel", choices=("gemm", "flash", "ln"))
+    ap.add_argument("kernel", choices=("gemm", "gemm_res", "flash", "ln"))
     ap.add_argument("dims", type=int, nargs="+")
     ap.add_argument("--gelu", action="store_true")
     ap.add_argument("--causal", action="store_true")
@@ -78,6 +78,15 @@ def main(argv=None):
         rate = 2.0 * m * n * k / (ms / 1e3) / 1e12
         print(f"gemm M={m} N={n} K={k} gelu={a.gelu} tile_n={a.tile_n} pair={a.pair}: {ms:.4f} ms  "
               f"{rate:.1f} TFLOP/s")
+    elif a.kernel == "gemm_res":
+        m, n, k = a.dims
+        x = torch.randn(m, k, device=dev).half()
+        w = (torch.randn(n, k, device=dev) / math.sqrt(k)).half()
+        b = torch.randn(n, device=dev)
+        xr = torch.randn(m, n, device=dev)
+        ms = T(lambda: K.linear_residual(x, w, b, xr, xr, tile_n=a.tile_n, pair=a.pair))
+        rate = 2.0 * m * n * k / (ms / 1e3) / 1e12
+        print(f"gemm_res M={m} N={n} K={k} tile_n={a.tile_n} pair={a.pair}: {ms:.4f} ms  {rate:.1f} TFLOP/s")
     elif a.kernel == "flash":
         bsz, h, s, hd = a.dims
         d = h * hd
