@@ -62,6 +62,10 @@ extern "C" {
 #define TF_ATTN_EXP_F32 4 /* fp32 exp2 for the probabilities (default: the
                              packed fp16 exp2 unit; P is rounded to fp16 for
                              the PV product either way) */
+/* flags bits 8..15: how many of the 64 probability pairs per row and key
+ * block are exponentiated on the FMA pipes instead of the exp unit
+ * (0, 16, 24 or 32; fp16 exp path only) */
+#define TF_ATTN_FMA_EXP_SHIFT 8
 
 /* ABI version, bumped on any signature change. */
 int tf_abi_version(void);

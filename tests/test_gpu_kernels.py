@@ -246,6 +246,30 @@ def test_flash_packed_qkv(K, b, h, sq, sk, hd, causal, masked, exp_f32):
     assert torch.allclose(lse[fin], lse_ref[fin], atol=2e-3, rtol=1e-4)
 
 
+@pytest.mark.parametrize("pairs", [16, 24, 32])
+@pytest.mark.parametrize("b,h,sq,hd,causal,masked", [(2, 4, 300, 64, True, True), (1, 2, 513, 128, False, False)])
+def test_flash_fma_exp(K, pairs, b, h, sq, hd, causal, masked):
+    """Part of the exponentials on the FMA pipes (binary16 built from a
+    polynomial) gives the same attention within the fp16-P tolerance."""
+    d = h * hd
+    qkv = _qkv(b, h, sq, hd, pairs + sq)
+    kv_valid = None
+    if masked:
+        kv_valid = torch.arange(sq)[None, :] < torch.tensor([sq - 37 * (i + 1) for i in range(b)])[:, None]
+    split = lambda t: t.reshape(b, sq, h, hd).transpose(1, 2)
+    ref, lse_ref = om.attention_fp16(split(qkv[..., :d]), split(qkv[..., d:2 * d]), split(qkv[..., 2 * d:]),
+                                     hd ** -0.5, causal, kv_valid)
+    ref = ref.transpose(1, 2).reshape(b, sq, d)
+    g = qkv.cuda()
+    out, lse = K.flash_attention(g[..., :d], g[..., d:2 * d], g[..., 2 * d:], h, hd ** -0.5, causal=causal,
+                                 key_valid=None if kv_valid is None else kv_valid.cuda(), want_lse=True,
+                                 fma_exp_pairs=pairs)
+    out = out.float().cpu()
+    assert torch.all((out - ref).abs() <= 1e-2 * ref.abs() + 3e-3), (out - ref).abs().max()
+    fin = torch.isfinite(lse_ref)
+    assert torch.allclose(lse.cpu()[fin], lse_ref[fin], atol=2e-3, rtol=1e-4)
+
+
 @pytest.mark.parametrize("hd", [64, 128])
 def test_flash_offsets_and_f32_out(K, hd):
     """Context-parallel block: queries at global positions [q0, q0+Sq), keys

@@ -65,26 +65,28 @@ struct AttnKParams {
 
 template <int HD>
 struct AttnCfg {
-  static constexpr bool kLFromMma = HD == 64;  // row sum from a ones column of V
-  static constexpr int kNO = kLFromMma ? HD + 16 : HD;  // O columns per tile
-  static constexpr int kKStages = HD == 64 ? 3 : 2;
-  static constexpr int kVStages = HD == 64 ? 3 : 1;
+  // S = Q K^T for successive (tile, key block) pairs goes round a ring of kNS
+  // TMEM slots; the softmax overwrites the first 64 columns of its slot with
+  // P (fp16 pairs), which the PV product reads straight from TMEM. A slot is
+  // reused by S of the pair kNS later, issued after that PV: the tensor core
+  // runs the MMAs of this thread in issue order.
+  static constexpr int kNS = HD == 64 ? 3 : 2;
+  static constexpr int kKStages = HD == 64 ? 4 : 2;
+  static constexpr int kVStages = HD == 64 ? 4 : 2;
   static constexpr int kTileBytes = 128 * HD * 2;  // a 128-row x HD fp16 tile
   static constexpr int kQOff = 0;
   static constexpr int kKOff = kQOff + kAttnTiles * kTileBytes;
   static constexpr int kVOff = kKOff + kKStages * kTileBytes;
-  static constexpr int kOnesOff = kVOff + kVStages * kTileBytes;
-  static constexpr int kPOff = kOnesOff + (kLFromMma ? 16384 : 0);
-  static constexpr int kPBytes = kAttnBM * kAttnBN * 2;
-  static constexpr int kBarOff = kPOff + kAttnTiles * kPBytes;
-  // q_full, k_full/empty[KS], v_full/empty[VS], s_full[2], s_free[2],
-  // p_full[2], o_full[2], turn[2], drain
-  static constexpr int kNumBars = 1 + 2 * kKStages + 2 * kVStages + 10 + 1;
+  static constexpr int kBarOff = kVOff + kVStages * kTileBytes;
+  // q_full, k_full/empty[KS], v_full/empty[VS], s_full[NS],
+  // p_full[2 tiles x 2 alternating], o_full[2], turn[2], drain
+  static constexpr int kNumBars = 1 + 2 * kKStages + 2 * kVStages + kNS + 4 + 2 + 2 + 1;
   static constexpr int kBytes = kBarOff + kNumBars * 8 + 16;
   static constexpr int kAlloc = kBytes + 1024;
-  // TMEM columns
-  static constexpr uint32_t kTmS = 0;    // S_t at t*128
-  static constexpr uint32_t kTmO = 256;  // O_t at 256 + t*128
+  // TMEM columns: S/P slots at 0, 128, ..; O_t at kNS*128 + t*HD (512 in all)
+  static constexpr uint32_t kTmS = 0;
+  static constexpr uint32_t kTmO = kNS * 128;
+  static_assert(kNS * 128 + kAttnTiles * HD <= 512, "TMEM budget");
 };
 
 __device__ __forceinline__ float ex2_f32(float x) {
@@ -112,6 +114,27 @@ __device__ __forceinline__ uint32_t ex2_f16x2(uint32_t h) {
   uint32_t r;
   asm("ex2.approx.f16x2 %0, %1;" : "=r"(r) : "r"(h));
   return r;
+}
+
+// 2^t as a binary16 bit pattern, computed on the FMA/integer pipes (not the
+// exp unit), for t <= 8 (t may be -inf). Cody-Waite style reduction t = n + f
+// with n = round-to-nearest(t - 1/2), f in [0, 1]; 2^f from a degree-3
+// minimax polynomial with p(0) = 1 (coefficients fitted for this library by a
+// Remez iteration; max relative error 8.6e-5, below half an fp16 ulp); then
+// the binary16 pattern (n + 15) * 1024 + round(1024 * 2^f) - 1024, where a
+// mantissa that rounds up to 2048 carries into the exponent field. Results
+// below 2^-14 (fp16 subnormals) flush to zero.
+__device__ __forceinline__ uint32_t exp2_f16_bits_fma(float t) {
+  const float kRound = 12582912.0f;  // 1.5 * 2^23: y = x + kRound keeps round(x) in the low bits of y
+  const float y = (t - 0.5f) + kRound;
+  const float f = t - (y - kRound);
+  float p = fmaf(f, 0.07706703990697861f, 0.22764499485492706f);
+  p = fmaf(p, f, 0.6951167583465576f);
+  p = fmaf(p, f, 1.0f);
+  const float q = fmaf(p, 1024.0f, kRound);  // low bits: round(1024 * p)
+  // (bits(y) - B) * 1024 + (bits(q) - B) + 14336, B = bits(kRound), mod 2^32
+  const uint32_t h = __float_as_uint(y) * 1024u + __float_as_uint(q) + (14336u - 0x4B400000u * 1025u);
+  return t < -14.0f ? 0u : (h & 0xFFFFu);
 }
 
 __device__ __forceinline__ uint32_t pack_f16x2_rn(float a, float b) {
@@ -166,7 +189,7 @@ __device__ __forceinline__ void rescale_o(uint32_t taddr, float alpha) {
   tmem_wait_st();
 }
 
-template <int HD, bool EXP16>
+template <int HD, bool EXP16, int POLY>
 __global__ void __launch_bounds__(kAttnThreads, 1)
     flash_fwd_tcgen05(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                       const __grid_constant__ CUtensorMap tmV, AttnKParams p) {
@@ -181,11 +204,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint64_t* k_empty = k_full + KS;
   uint64_t* v_full = k_empty + KS;
   uint64_t* v_empty = v_full + VS;
+  constexpr int NS = C::kNS;
   uint64_t* s_full = v_empty + VS;
-  uint64_t* s_free = s_full + 2;
-  uint64_t* p_full = s_free + 2;
-  uint64_t* o_full = p_full + 2;
-  uint64_t* turn = o_full + 2;  // exp-phase hand-off between the two softmax warpgroups
+  uint64_t* p_full = s_full + NS;  // [tile * 2 + (block & 1)]: alternating, so no waiter falls two phases behind
+  uint64_t* o_full = p_full + 4;   // [tile]: every PV of the tile so far has landed in O
+  uint64_t* turn = o_full + 2;     // exp-phase hand-off between the two softmax warpgroups
   uint64_t* drain = turn + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
 
@@ -211,6 +234,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     nblk[t] = k_end <= 0 ? 0 : static_cast<int>((k_end + kAttnBN - 1) / kAttnBN);
   }
   const int nmax = nblk[0] > nblk[1] ? nblk[0] : nblk[1];
+  // (tile, key block) pairs in issue order: (0, j), (1, j) while both tiles
+  // need block j, then the longer tile alone
+  const int nmin = nblk[0] < nblk[1] ? nblk[0] : nblk[1];
+  const int t_long = nblk[0] > nblk[1] ? 0 : 1;
+  const int n_pairs = nblk[0] + nblk[1];
 
   if (warp == 0 && lane == 0) {
     tma_prefetch_map(&tmQ);
@@ -225,30 +253,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       mbar_init(&v_full[s], 1);
       mbar_init(&v_empty[s], 1);
     }
+    for (int i = 0; i < NS; ++i) mbar_init(&s_full[i], 1);
+    for (int i = 0; i < 4; ++i) mbar_init(&p_full[i], 128);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&s_full[i], 1);
-      mbar_init(&s_free[i], 128);
-      mbar_init(&p_full[i], 128);
       mbar_init(&o_full[i], 1);
       mbar_init(&turn[i], 128);
     }
     mbar_init(drain, 1);
     fence_mbar_init();
-  }
-  if constexpr (C::kLFromMma) {
-    // constant "ones" column block: MN-major 128B-swizzled rows of 64 values,
-    // value index 0 (the first head_dim column past V) = 1.0, the rest 0
-    if (warp >= 4) {
-      const int r = threadIdx.x - 128;  // 0..255 -> rows 0..127 (two threads per row)
-      if (r < 256) {
-        const int row = r >> 1;
-        uint4* dst = reinterpret_cast<uint4*>(smem + C::kOnesOff + row * 128);
-#pragma unroll
-        for (int c = (r & 1) * 4; c < (r & 1) * 4 + 4; ++c)
-          dst[c] = make_uint4(c == (row & 7) ? 0x3C00u : 0u, 0u, 0u, 0u);
-      }
-      fence_proxy_async_smem();
-    }
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, 512);
@@ -303,66 +315,63 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   } else if (warp == 1) {
     if (lane == 0 && nmax > 0) {
       // ---------------- MMA issuer ----------------
-      constexpr uint32_t idesc_s = idesc_f16_f32(kAttnBM, kAttnBN);           // K-major Q, K-major K
-      constexpr uint32_t idesc_o = idesc_f16_f32(kAttnBM, C::kNO, false, true);  // K-major P, MN-major V
+      constexpr uint32_t idesc_s = idesc_f16_f32(kAttnBM, kAttnBN);     // K-major Q, K-major K
+      constexpr uint32_t idesc_o = idesc_f16_f32(kAttnBM, HD, false, true);  // K-major P, MN-major V
       const uint32_t sbase = smem_u32(smem);
-      auto issue_s = [&](int t, int j) {
+      auto pair_of = [&](int q, int& t, int& j) {
+        if (q < 2 * nmin) {
+          j = q >> 1;
+          t = q & 1;
+        } else {
+          j = nmin + (q - 2 * nmin);
+          t = t_long;
+        }
+      };
+      // the last pair (in issue order) that reads key block j
+      auto last_user = [&](int t, int j) { return t == 1 || j >= nblk[1]; };
+      auto issue_s = [&](int q) -> bool {
+        int t, j;
+        pair_of(q, t, j);
+        const int slot = q % NS;
+        // the slot's previous P (pair q - NS) was consumed by a PV issued
+        // before this point, hence executed before these MMAs
+        if (!mbar_wait(&k_full[j % KS], (j / KS) & 1, p.status, kDevTimeoutMma)) return false;
+        tc_fence_after();
         const uint32_t qa = sbase + C::kQOff + t * C::kTileBytes;
         const uint32_t ka = sbase + C::kKOff + (j % KS) * C::kTileBytes;
 #pragma unroll
         for (int k = 0; k < HD / 16; ++k) {
           const uint32_t off = (k >> 2) * 16384 + (k & 3) * 32;
-          umma_f16_ss(tmem_base + C::kTmS + t * 128, smem_desc_sw128(qa + off, 16, 1024),
+          umma_f16_ss(tmem_base + C::kTmS + slot * 128, smem_desc_sw128(qa + off, 16, 1024),
                       smem_desc_sw128(ka + off, 16, 1024), idesc_s, k > 0 ? 1u : 0u);
         }
-        umma_commit(&s_full[t]);
+        umma_commit(&s_full[slot]);
+        if (last_user(t, j)) umma_commit(&k_empty[j % KS]);
+        return true;
       };
-      auto issue_pv = [&](int t, int j) {
-        const uint32_t pa = sbase + C::kPOff + t * C::kPBytes;
-        const uint32_t va = sbase + C::kVOff + (j % VS) * C::kTileBytes;
-        // MN-major V: 8-key groups at 1024 B (SBO); the second 64-wide column
-        // block (head_dim 128, or the ones block) at LBO
-        const uint32_t lbo = C::kLFromMma ? (sbase + C::kOnesOff - va) : 16384u;
-#pragma unroll
-        for (int k = 0; k < kAttnBN / 16; ++k) {
-          umma_f16_ss(tmem_base + C::kTmO + t * 128,
-                      smem_desc_sw128(pa + (k >> 2) * 16384 + (k & 3) * 32, 16, 1024),
-                      smem_desc_sw128(va + k * 2048, lbo, 1024), idesc_o, (j > 0 || k > 0) ? 1u : 0u);
-        }
-        umma_commit(&o_full[t]);
-      };
-      bool ok = mbar_wait(q_full, 0, p.status, kDevTimeoutMma) &&
-                mbar_wait(&k_full[0], 0, p.status, kDevTimeoutMma);
-      if (ok) {
+      auto issue_pv = [&](int q) -> bool {
+        int t, j;
+        pair_of(q, t, j);
+        const int slot = q % NS;
+        if (!mbar_wait(&v_full[j % VS], (j / VS) & 1, p.status, kDevTimeoutMma)) return false;
+        if (!mbar_wait(&p_full[t * 2 + (j & 1)], (j >> 1) & 1, p.status, kDevTimeoutMma)) return false;
         tc_fence_after();
-        for (int t = 0; t < kAttnTiles; ++t)
-          if (nblk[t] > 0) issue_s(t, 0);
-        umma_commit(&k_empty[0]);
-      }
-      for (int j = 0; j < nmax && ok; ++j) {
-        if (j + 1 < nmax) {
-          const int s = (j + 1) % KS;
-          if (!(ok = mbar_wait(&k_full[s], ((j + 1) / KS) & 1, p.status, kDevTimeoutMma))) break;
-          for (int t = 0; t < kAttnTiles && ok; ++t) {
-            if (j + 1 < nblk[t]) {
-              if (!(ok = mbar_wait(&s_free[t], j & 1, p.status, kDevTimeoutMma))) break;
-              tc_fence_after();
-              issue_s(t, j + 1);
-            }
-          }
-          if (!ok) break;
-          umma_commit(&k_empty[s]);
-        }
-        if (!(ok = mbar_wait(&v_full[j % VS], (j / VS) & 1, p.status, kDevTimeoutMma))) break;
-        for (int t = 0; t < kAttnTiles && ok; ++t) {
-          if (j < nblk[t]) {
-            if (!(ok = mbar_wait(&p_full[t], j & 1, p.status, kDevTimeoutMma))) break;
-            tc_fence_after();
-            issue_pv(t, j);
-          }
-        }
-        if (!ok) break;
-        umma_commit(&v_empty[j % VS]);
+        const uint32_t va = sbase + C::kVOff + (j % VS) * C::kTileBytes;
+        // P: 128 keys = 64 TMEM columns, 8 per MMA; V: MN-major, 8-key groups
+        // at 1024 B (SBO), 64-wide head-dim blocks at 16 KB (LBO)
+#pragma unroll
+        for (int k = 0; k < kAttnBN / 16; ++k)
+          umma_f16_ts(tmem_base + C::kTmO + t * HD, tmem_base + C::kTmS + slot * 128 + k * 8,
+                      smem_desc_sw128(va + k * 2048, 16384, 1024), idesc_o, (j > 0 || k > 0) ? 1u : 0u);
+        umma_commit(&o_full[t]);
+        if (last_user(t, j)) umma_commit(&v_empty[j % VS]);
+        return true;
+      };
+      bool ok = mbar_wait(q_full, 0, p.status, kDevTimeoutMma);
+      for (int q = 0; q < NS && q < n_pairs && ok; ++q) ok = issue_s(q);
+      for (int q = 0; q < n_pairs && ok; ++q) {
+        ok = issue_pv(q);
+        if (ok && q + NS < n_pairs) ok = issue_s(q + NS);
       }
       umma_commit(drain);
       mbar_wait(drain, 0, p.status, kDevTimeoutDrain);
@@ -376,32 +385,31 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const int r = quarter * 32 + lane;  // row within the tile
     const int row = q0 + t * kAttnBM + r;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
-    const uint32_t tm_s = tmem_base + lane_off + C::kTmS + t * 128;
-    const uint32_t tm_o = tmem_base + lane_off + C::kTmO + t * 128;
+    const uint32_t tm_s = tmem_base + lane_off + C::kTmS;
+    const uint32_t tm_o = tmem_base + lane_off + C::kTmO + t * HD;
     const long long q_glob = p.q_pos0 + row;
     const uint8_t* kvalid = p.key_valid ? p.key_valid + static_cast<long long>(b) * p.seq_k : nullptr;
-    uint8_t* prow = smem + C::kPOff + t * C::kPBytes + r * 128;
     const int nb = nblk[t];
-    const int n_pp = nblk[0] < nblk[1] ? nblk[0] : nblk[1];  // blocks where both tiles take turns
+    const int n_pp = nmin;  // blocks where both tiles take turns
     const float c = p.scale_log2;
 
     float m_ref = -INFINITY;  // reference max (scaled log2 domain)
-    float l = 0.f;            // row sum (when not produced by the MMA)
+    float l = 0.f;            // row sum
     bool ok = true;
 
     for (int j = 0; j < nb; ++j) {
-      if (!(ok = mbar_wait(&s_full[t], j & 1, p.status, kDevTimeoutSoftmax))) break;
+      const int q = j < nmin ? 2 * j + t : 2 * nmin + (j - nmin);  // issue order of (t, j)
+      const int slot = q % NS;
+      if (!(ok = mbar_wait(&s_full[slot], (q / NS) & 1, p.status, kDevTimeoutSoftmax))) break;
       tc_fence_after();
       float s[128];
       {
         uint32_t v[128];
-        tmem_ld128(tm_s, v);  // the whole S row in one load, one wait
+        tmem_ld128(tm_s + slot * 128, v);  // the whole S row in one load, one wait
         tmem_wait_ld();
 #pragma unroll
         for (int i = 0; i < 128; ++i) s[i] = __uint_as_float(v[i]);
       }
-      tc_fence_before();
-      mbar_arrive(&s_free[t]);
 
       // ---- masking (tails, causal diagonal, key padding) ----
       const long long kbase = static_cast<long long>(j) * kAttnBN;
@@ -463,9 +471,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       } else if (__any_sync(0xffffffffu, need)) {
         const float m_new = fmaxf(m_ref, m_row);
         const float alpha = m_ref == -INFINITY ? 0.f : ex2_f32(m_ref - m_new);
+        // every PV so far (the last is block j-1) must have landed in O
         if (!(ok = mbar_wait(&o_full[t], (j - 1) & 1, p.status, kDevTimeoutSoftmax))) break;
         tc_fence_after();
-        rescale_o<C::kNO>(tm_o, alpha);
+        rescale_o<HD>(tm_o, alpha);
         l *= alpha;
         m_ref = m_new;
       }
@@ -486,16 +495,18 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 #pragma unroll
       for (int i = 0; i < 128; ++i) s[i] = fmaf(s[i], c, -m_use);
       if constexpr (EXP16) {
+        // POLY of the 64 pairs on the FMA pipes, the rest on the exp unit
 #pragma unroll
-        for (int i = 0; i < 64; ++i) pk[i] = pack_f16x2_rn(s[2 * i], s[2 * i + 1]);
+        for (int i = POLY; i < 64; ++i) pk[i] = pack_f16x2_rn(s[2 * i], s[2 * i + 1]);
 #pragma unroll
-        for (int i = 0; i < 64; ++i) pk[i] = ex2_f16x2(pk[i]);
-        if constexpr (!C::kLFromMma) {
+        for (int i = POLY; i < 64; ++i) pk[i] = ex2_f16x2(pk[i]);
 #pragma unroll
-          for (int i = 0; i < 64; ++i) {
-            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&pk[i]));
-            ls[i & 7] += f.x + f.y;
-          }
+        for (int i = 0; i < POLY; ++i)
+          pk[i] = exp2_f16_bits_fma(s[2 * i]) | (exp2_f16_bits_fma(s[2 * i + 1]) << 16);
+#pragma unroll
+        for (int i = 0; i < 64; ++i) {
+          const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&pk[i]));
+          ls[i & 7] += f.x + f.y;
         }
       } else {
 #pragma unroll
@@ -503,58 +514,38 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 #pragma unroll
         for (int i = 0; i < 64; ++i) {
           pk[i] = pack_f16x2_rn(s[2 * i], s[2 * i + 1]);
-          if constexpr (!C::kLFromMma) ls[i & 7] += s[2 * i] + s[2 * i + 1];
+          ls[i & 7] += s[2 * i] + s[2 * i + 1];
         }
       }
-      if constexpr (!C::kLFromMma) l += ((ls[0] + ls[1]) + (ls[2] + ls[3])) + ((ls[4] + ls[5]) + (ls[6] + ls[7]));
+      l += ((ls[0] + ls[1]) + (ls[2] + ls[3])) + ((ls[4] + ls[5]) + (ls[6] + ls[7]));
       if (j < n_pp) mbar_arrive(&turn[1 - t]);
 
-      // P buffer is free once PV of block j-1 has completed
-      if (j > 0) {
-        if (!(ok = mbar_wait(&o_full[t], (j - 1) & 1, p.status, kDevTimeoutSoftmax))) break;
-      }
-#pragma unroll
-      for (int ch = 0; ch < 16; ++ch) {
-        const int blk = ch >> 3;
-        const int cc = (ch & 7) ^ (r & 7);
-        *reinterpret_cast<uint4*>(prow + blk * 16384 + cc * 16) =
-            make_uint4(pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]);
-      }
-      fence_proxy_async_smem();
+      // P into the first 64 columns of this pair's S slot (already read)
+      tmem_st64(tm_s + slot * 128, pk);
+      tmem_wait_st_all();
       tc_fence_before();
-      mbar_arrive(&p_full[t]);
+      mbar_arrive(&p_full[t * 2 + (j & 1)]);
     }
 
     // ---------------- epilogue ----------------
     if (ok) {
       float inv = 0.f;
-      uint32_t ov[C::kNO];
+      uint32_t ov[HD];
       if (nb > 0) {
         if (!(ok = mbar_wait(&o_full[t], (nb - 1) & 1, p.status, kDevTimeoutSoftmax))) {
           // fall through to the barrier; nothing is written
         } else {
           tc_fence_after();
           if constexpr (HD == 128) {
-            uint32_t v[128];
-            tmem_ld128(tm_o, v);
-            tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 128; ++i) ov[i] = v[i];
+            tmem_ld128(tm_o, ov);
           } else {
-            uint32_t v[64], w[16];
-            tmem_ld64(tm_o, v);
-            tmem_ld16(tm_o + 64, w);
-            tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 64; ++i) ov[i] = v[i];
-#pragma unroll
-            for (int i = 0; i < 16; ++i) ov[64 + i] = w[i];
+            tmem_ld64(tm_o, ov);
           }
-          if constexpr (C::kLFromMma) l = __uint_as_float(ov[HD]);
+          tmem_wait_ld();
         }
       } else {
 #pragma unroll
-        for (int i = 0; i < C::kNO; ++i) ov[i] = 0u;
+        for (int i = 0; i < HD; ++i) ov[i] = 0u;
       }
       if (ok && row < p.seq_q) {
         inv = l > 0.f ? 1.f / l : 0.f;
@@ -626,11 +617,11 @@ __global__ void attn_merge_kernel(float* __restrict__ o_acc, float* __restrict__
 // host side
 // ---------------------------------------------------------------------------
 
-template <int HD, bool EXP16>
+template <int HD, bool EXP16, int POLY>
 static int launch_flash(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                         const AttnKParams& kp, dim3 grid, cudaStream_t stream) {
   using C = AttnCfg<HD>;
-  auto kern = flash_fwd_tcgen05<HD, EXP16>;
+  auto kern = flash_fwd_tcgen05<HD, EXP16, POLY>;
   static bool attr_done[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -699,11 +690,24 @@ int flash_fwd(const AttnArgs& a, cudaStream_t stream) {
   if (kp.status == nullptr) return last_error_code();
   dim3 grid(kp.q_blocks, static_cast<unsigned>(a.heads), static_cast<unsigned>(a.batch));
   const bool exp16 = !(a.flags & TF_ATTN_EXP_F32);
-  if (a.head_dim == 64)
-    return exp16 ? launch_flash<64, true>(tq, tk, tv, kp, grid, stream)
-                 : launch_flash<64, false>(tq, tk, tv, kp, grid, stream);
-  return exp16 ? launch_flash<128, true>(tq, tk, tv, kp, grid, stream)
-               : launch_flash<128, false>(tq, tk, tv, kp, grid, stream);
+  // pairs per row whose exponentials run on the FMA pipes (flags bits 8..15)
+  const int poly = (a.flags >> 8) & 0xFF;
+  if (poly != 0 && poly != 16 && poly != 24 && poly != 32)
+    return set_error(TF_ERR_SHAPE, "flash: FMA-pipe exp pairs must be 0, 16, 24 or 32");
+  if (!exp16) {
+    return a.head_dim == 64 ? launch_flash<64, false, 0>(tq, tk, tv, kp, grid, stream)
+                            : launch_flash<128, false, 0>(tq, tk, tv, kp, grid, stream);
+  }
+#define TFB_FLASH_POLY(P)                                                          \
+  return a.head_dim == 64 ? launch_flash<64, true, P>(tq, tk, tv, kp, grid, stream) \
+                          : launch_flash<128, true, P>(tq, tk, tv, kp, grid, stream);
+  switch (poly) {
+    case 16: TFB_FLASH_POLY(16)
+    case 24: TFB_FLASH_POLY(24)
+    case 32: TFB_FLASH_POLY(32)
+    default: TFB_FLASH_POLY(0)
+  }
+#undef TFB_FLASH_POLY
 }
 
 int attn_merge(const MergeArgs& a, cudaStream_t stream) {

@@ -68,16 +68,30 @@ struct GemmSmem {
 // ways) so that the global accesses run along rows: lane L handles columns
 // 4*(L%8)..+3 of rows it*4 + L/8, i.e. each store instruction covers 4 rows
 // x 64 B (fp16) or 4 rows x 128 B (fp32) instead of 32 scattered rows.
+// Residual rows of one chunk for this lane (EPI 2): rows row0 + it*4 + L/8,
+// columns col0 + 4*(L%8), it = 0..7. Issued ahead of use so the HBM latency
+// overlaps the previous chunk.
+__device__ __forceinline__ void load_residual(const GemmArgs& p, float4 (&xv)[8], int row0, int col0) {
+  const int lane = threadIdx.x & 31;
+  const int c4 = (lane & 7) * 4;
+#pragma unroll
+  for (int it = 0; it < 8; ++it) {
+    const int row = row0 + it * 4 + (lane >> 3);
+    xv[it] = row < p.M ? __ldcs(reinterpret_cast<const float4*>(p.x_in + static_cast<long long>(row) * p.ldx + col0 + c4))
+                       : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+}
+
 template <int EPI>
 __device__ __forceinline__ void epilogue_chunk(const GemmArgs& p, const uint32_t (&r)[32], float* buf, int row0,
-                                               int col0) {
+                                               int col0, const float4 (&xv)[8]) {
   const int lane = threadIdx.x & 31;
 #pragma unroll
   for (int i = 0; i < 32; ++i) buf[lane * 33 + i] = __uint_as_float(r[i]);
   __syncwarp();
   const int c4 = (lane & 7) * 4;
   const float4 bq = __ldg(reinterpret_cast<const float4*>(p.bias + col0 + c4));
-#pragma unroll 2
+#pragma unroll
   for (int it = 0; it < 8; ++it) {
     const int rl = it * 4 + (lane >> 3);
     const int row = row0 + rl;
@@ -86,11 +100,10 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& p, const uint32_t
     if (row < p.M) {
       if constexpr (EPI == 2) {
         const long long off = static_cast<long long>(row) * p.ldx + col0 + c4;
-        const float4 xv = *reinterpret_cast<const float4*>(p.x_in + off);
         bool valid = true;
         if (p.mask_mode != 0) valid = p.valid[row] != 0;
         if (p.mask_mode == 1 && !valid) v0 = v1 = v2 = v3 = 0.f;
-        float4 o = make_float4(xv.x + v0, xv.y + v1, xv.z + v2, xv.w + v3);
+        float4 o = make_float4(xv[it].x + v0, xv[it].y + v1, xv[it].z + v2, xv[it].w + v3);
         if (p.mask_mode == 2 && !valid) o = make_float4(0.f, 0.f, 0.f, 0.f);
         *reinterpret_cast<float4*>(p.x_out + off) = o;
       } else {
@@ -232,6 +245,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tc_fence_after();
       const int row0 = m0 + quarter * 32;
       const uint32_t t_addr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + a * BN;
+      float4 xa[8], xb[8];
+      if constexpr (EPI == 2) {
+        if (row0 < p.M) load_residual(p, xa, row0, n0);
+      }
       uint32_t r0[32], r1[32];
       tmem_ld32(t_addr, r0);
 #pragma unroll
@@ -239,15 +256,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         tmem_wait_ld();
         uint32_t(&cur)[32] = (c & 1) ? r1 : r0;
         uint32_t(&nxt)[32] = (c & 1) ? r0 : r1;
+        float4(&xcur)[8] = (c & 1) ? xb : xa;
+        float4(&xnxt)[8] = (c & 1) ? xa : xb;
         if (c + 1 < BN / 32) {
           tmem_ld32(t_addr + (c + 1) * 32, nxt);
+          if constexpr (EPI == 2) {
+            if (row0 < p.M && n0 + (c + 1) * 32 < p.N) load_residual(p, xnxt, row0, n0 + (c + 1) * 32);
+          }
         } else {
           // accumulator fully read: hand the buffer back to the MMA warp
           tc_fence_before();
           mbar_arrive(&tempty[a]);
         }
         const int col0 = n0 + c * 32;
-        if (col0 < p.N && row0 < p.M) epilogue_chunk<EPI>(p, cur, ebuf, row0, col0);
+        if (col0 < p.N && row0 < p.M) epilogue_chunk<EPI>(p, cur, ebuf, row0, col0, xcur);
       }
     }
   }
@@ -415,6 +437,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemm2Threads, 1)
       const int row0 = m0 + quarter * 32;
       const uint32_t t_addr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + a * BN + half * (BN / 2);
       constexpr int NCH = BN / 64;  // 32-column chunks per half
+      float4 xa[8], xb[8];
+      if constexpr (EPI == 2) {
+        if (row0 < p.M) load_residual(p, xa, row0, n0);
+      }
       uint32_t r0[32], r1[32];
       tmem_ld32(t_addr, r0);
 #pragma unroll
@@ -422,8 +448,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemm2Threads, 1)
         tmem_wait_ld();
         uint32_t(&cur)[32] = (c & 1) ? r1 : r0;
         uint32_t(&nxt)[32] = (c & 1) ? r0 : r1;
+        float4(&xcur)[8] = (c & 1) ? xb : xa;
+        float4(&xnxt)[8] = (c & 1) ? xa : xb;
         if (c + 1 < NCH) {
           tmem_ld32(t_addr + (c + 1) * 32, nxt);
+          if constexpr (EPI == 2) {
+            if (row0 < p.M && n0 + (c + 1) * 32 < p.N) load_residual(p, xnxt, row0, n0 + (c + 1) * 32);
+          }
         } else {
           // accumulator fully read: hand the buffer back to the leader's MMA
           tc_fence_before();
@@ -431,7 +462,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemm2Threads, 1)
           if (lane == 0) mbar_arrive_cluster(tempty_leader + a * 8);
         }
         const int col0 = n0 + c * 32;
-        if (col0 < p.N && row0 < p.M) epilogue_chunk<EPI>(p, cur, ebuf, row0, col0);
+        if (col0 < p.N && row0 < p.M) epilogue_chunk<EPI>(p, cur, ebuf, row0, col0, xcur);
       }
     }
   }
@@ -552,7 +583,8 @@ int gemm_f16(const GemmCall& g, cudaStream_t stream) {
       const long long mt = (M + 255) / 256;
       const long long c256 = mt * (N / 256), c128 = mt * (N / 128);
       const int nc = sms / 2;
-      if (1.1 * double((c128 + nc - 1) / nc) < 2.0 * double((c256 + nc - 1) / nc)) bn = 128;
+      // a 128-wide pair tile costs ~0.6 of a 256-wide one (measured)
+      if (1.25 * double((c128 + nc - 1) / nc) < 2.0 * double((c256 + nc - 1) / nc)) bn = 128;
     }
   }
 

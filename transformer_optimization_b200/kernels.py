@@ -155,7 +155,8 @@ def linear_residual(a: torch.Tensor, w: torch.Tensor, b: torch.Tensor, x_in: tor
 def flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, heads: int, scale: float, *,
                     causal: bool = False, key_valid: Optional[torch.Tensor] = None, q_pos0: int = 0,
                     k_pos0: int = 0, out: Optional[torch.Tensor] = None, out_dtype: torch.dtype = torch.float16,
-                    lse: Optional[torch.Tensor] = None, want_lse: bool = False, exp_f32: bool = False):
+                    lse: Optional[torch.Tensor] = None, want_lse: bool = False, exp_f32: bool = False,
+                    fma_exp_pairs: int = 0):
     """Flash attention forward (tf_flash_fwd).
 
     q: [B, Sq, H*hd] fp16 view with unit inner stride (may be a column slice
@@ -186,6 +187,7 @@ def flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, heads: in
     flags = (_abi.TF_ATTN_CAUSAL if causal else 0) | (_abi.TF_ATTN_OUT_F32 if out_dtype == torch.float32 else 0)
     if exp_f32:
         flags |= _abi.TF_ATTN_EXP_F32
+    flags |= (int(fma_exp_pairs) & 0xFF) << 8
     _abi.call("tf_flash_fwd", _ptr(q), _ptr(k), _ptr(v), q.stride(1), k.stride(1), q.stride(0), k.stride(0),
               _ptr(out), out.stride(1), out.stride(0), _ptr(lse), _ptr(key_valid), bsz, heads, sq, sk, hd,
               float(scale), int(q_pos0), int(k_pos0), flags, _stream())
