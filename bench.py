@@ -182,6 +182,12 @@ def kernel_profile(model, x):
     try:
         model.use_cuda_graphs = False
         with torch.inference_mode():
+            # the first eager pass warms the allocator's pools for the eager
+            # buffers (a cudaMalloc between two events would be timed)
+            model(x)
+            torch.cuda.synchronize()
+            for lst in rec.values():
+                lst.clear()
             model(x)
         torch.cuda.synchronize()
     finally:

@@ -59,12 +59,12 @@ extern "C" {
 /* tf_flash_fwd flags */
 #define TF_ATTN_CAUSAL 1  /* mask key position > query position */
 #define TF_ATTN_OUT_F32 2 /* out is fp32 (default fp16) */
-#define TF_ATTN_EXP_F32 4 /* fp32 exp2 for the probabilities (default: the
-                             packed fp16 exp2 unit; P is rounded to fp16 for
-                             the PV product either way) */
+#define TF_ATTN_EXP_F16X2 4 /* packed fp16 exp2 for the probabilities (default:
+                               fp32 exp2, the faster of the two on B200; P is
+                               rounded to fp16 for the PV product either way) */
 /* flags bits 8..15: how many of the 64 probability pairs per row and key
  * block are exponentiated on the FMA pipes instead of the exp unit
- * (0, 16, 24 or 32; fp16 exp path only) */
+ * (0, 16, 24 or 32; packed fp16 exp path only) */
 #define TF_ATTN_FMA_EXP_SHIFT 8
 
 /* ABI version, bumped on any signature change. */

@@ -41,7 +41,7 @@ TF_RES_MASK_X = 2
 
 TF_ATTN_CAUSAL = 1
 TF_ATTN_OUT_F32 = 2
-TF_ATTN_EXP_F32 = 4
+TF_ATTN_EXP_F16X2 = 4
 
 # every symbol include/tfb200.h declares, with its ctypes signature
 _P = ctypes.c_void_p

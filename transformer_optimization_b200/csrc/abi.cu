@@ -156,7 +156,7 @@ static inline int begin_call() {
 
 extern "C" {
 
-int tf_abi_version(void) { return 4; }
+int tf_abi_version(void) { return 5; }
 
 const char* tf_last_error(void) { return tfb::g_msg; }
 

@@ -5,8 +5,8 @@
 // Replaces the attention of the reference's fp32-model fast path
 // (F.scaled_dot_product_attention / _short_attn_kernel / _flash_attn_kernel,
 // torch_transformer_benchmark.py:4146-4161, 1193-1418). Like the reference's
-// flash kernel it never materialises the score matrix: scores live in TMEM,
-// probabilities in shared memory, one 128-key block at a time, with a running
+// flash kernel it never materialises the score matrix: scores and
+// probabilities live in TMEM, one 128-key block at a time, with a running
 // max per query row and exp2 with the scale folded into log2(e)
 // (torch_transformer_benchmark.py:1427-1428).
 //
@@ -16,19 +16,22 @@
 //   warp 2        TMA producer of the V_j blocks
 //   warps 4..7    softmax of tile 0 (thread = query row)
 //   warps 8..11   softmax of tile 1
-// Per key block j and tile t the MMA thread issues
-//   S_t = Q_t K_j^T   -> TMEM (fp32, 128 columns)
-//   O_t += P_t V_j    -> TMEM (fp32, accumulated over all blocks)
-// and the two softmax warpgroups alternate, so one tile's exponentials run
-// while the tensor core works on the other tile.
+// Per key block j and tile t (a "pair" q, issued in the order t0 j0, t1 j0,
+// t0 j1, ...) the MMA thread issues
+//   S_q = Q_t K_j^T   -> one of NS TMEM slots (fp32, 128 columns)
+//   O_t += P_q V_j    -> TMEM (fp32, accumulated over all blocks), with P_q
+//                        read from TMEM (tcgen05.mma A-from-TMEM form)
+// in the order S_0 .. S_{NS-1}, then PV_q, S_{q+NS} for each q. The softmax
+// writes P_q as packed fp16 over the first 64 columns of S_q's slot, so a
+// slot is free again once PV_q has been issued (the tensor core executes in
+// issue order). The two softmax warpgroups take turns for the exponentials,
+// so one tile's exp phase overlaps the other tile's TMEM load and row max.
 //
 // Online softmax with lazy rescaling: a row keeps a reference max m; P =
 // exp2(s*c - m) is computed against it, and O (and l) are rescaled in TMEM
 // only when the row max grows by more than 8 (log2 units), so P <= 2^8 stays
-// well inside fp16. The final O/l is the exact softmax either way.
-// For head_dim 64 the row sum l comes out of the tensor core: V is extended
-// by a constant column block whose first column is 1.0, so O column 64 holds
-// sum_j P_j, computed from exactly the fp16 P that multiplies V.
+// well inside fp16. The final O/l is the exact softmax either way. The row
+// sum l adds the fp32 probabilities before their rounding to fp16.
 //
 // The kernel also emits the natural-log sum-exp per row, used to merge the
 // partial results of context-parallel ring attention exactly.
@@ -689,11 +692,12 @@ int flash_fwd(const AttnArgs& a, cudaStream_t stream) {
   kp.status = device_status_ptr();
   if (kp.status == nullptr) return last_error_code();
   dim3 grid(kp.q_blocks, static_cast<unsigned>(a.heads), static_cast<unsigned>(a.batch));
-  const bool exp16 = !(a.flags & TF_ATTN_EXP_F32);
+  const bool exp16 = (a.flags & TF_ATTN_EXP_F16X2) != 0;
   // pairs per row whose exponentials run on the FMA pipes (flags bits 8..15)
   const int poly = (a.flags >> 8) & 0xFF;
   if (poly != 0 && poly != 16 && poly != 24 && poly != 32)
     return set_error(TF_ERR_SHAPE, "flash: FMA-pipe exp pairs must be 0, 16, 24 or 32");
+  if (poly != 0 && !exp16) return set_error(TF_ERR_SHAPE, "flash: FMA-pipe exp pairs need TF_ATTN_EXP_F16X2");
   if (!exp16) {
     return a.head_dim == 64 ? launch_flash<64, false, 0>(tq, tk, tv, kp, grid, stream)
                             : launch_flash<128, false, 0>(tq, tk, tv, kp, grid, stream);

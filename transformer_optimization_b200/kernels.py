@@ -155,7 +155,7 @@ def linear_residual(a: torch.Tensor, w: torch.Tensor, b: torch.Tensor, x_in: tor
 def flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, heads: int, scale: float, *,
                     causal: bool = False, key_valid: Optional[torch.Tensor] = None, q_pos0: int = 0,
                     k_pos0: int = 0, out: Optional[torch.Tensor] = None, out_dtype: torch.dtype = torch.float16,
-                    lse: Optional[torch.Tensor] = None, want_lse: bool = False, exp_f32: bool = False,
+                    lse: Optional[torch.Tensor] = None, want_lse: bool = False, exp_f16x2: bool = False,
                     fma_exp_pairs: int = 0):
     """Flash attention forward (tf_flash_fwd).
 
@@ -185,8 +185,8 @@ def flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, heads: in
             raise ValueError("flash_attention: key_valid must be bool [B, Sk]")
         key_valid = key_valid.contiguous()
     flags = (_abi.TF_ATTN_CAUSAL if causal else 0) | (_abi.TF_ATTN_OUT_F32 if out_dtype == torch.float32 else 0)
-    if exp_f32:
-        flags |= _abi.TF_ATTN_EXP_F32
+    if exp_f16x2 or fma_exp_pairs:
+        flags |= _abi.TF_ATTN_EXP_F16X2
     flags |= (int(fma_exp_pairs) & 0xFF) << 8
     _abi.call("tf_flash_fwd", _ptr(q), _ptr(k), _ptr(v), q.stride(1), k.stride(1), q.stride(0), k.stride(0),
               _ptr(out), out.stride(1), out.stride(0), _ptr(lse), _ptr(key_valid), bsz, heads, sq, sk, hd,

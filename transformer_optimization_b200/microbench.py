@@ -57,7 +57,7 @@ def main(argv=None):
     ap.add_argument("dims", type=int, nargs="+")
     ap.add_argument("--gelu", action="store_true")
     ap.add_argument("--causal", action="store_true")
-    ap.add_argument("--exp-f32", action="store_true", help="flash: fp32 exp2 path")
+    ap.add_argument("--exp-f16x2", action="store_true", help="flash: packed fp16 exp2 path")
     ap.add_argument("--fma-exp", type=int, default=0, help="flash: pairs per row exponentiated on the FMA pipes")
     ap.add_argument("--tile-n", type=int, default=0)
     ap.add_argument("--pair", type=int, default=0, help="0 auto, 1 one-CTA tiles, 2 two-SM tiles")
@@ -94,7 +94,7 @@ def main(argv=None):
         qkv = torch.randn(bsz, s, 3 * d, device=dev).half()
         out = torch.empty(bsz, s, d, device=dev, dtype=torch.float16)
         ms = T(lambda: K.flash_attention(qkv[..., :d], qkv[..., d:2 * d], qkv[..., 2 * d:], h, hd ** -0.5,
-                                         causal=a.causal, out=out, exp_f32=a.exp_f32,
+                                         causal=a.causal, out=out, exp_f16x2=a.exp_f16x2,
                                          fma_exp_pairs=a.fma_exp))
         flops = 4.0 * bsz * s * s * d * (0.5 if a.causal else 1.0)
         print(f"flash B={bsz} H={h} S={s} hd={hd} causal={a.causal}: {ms:.4f} ms  "
