@@ -142,6 +142,16 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
 
 // Generic-proxy writes to shared memory -> visible to the async proxy
 // (tcgen05.mma operand reads).
+// Contiguous global -> shared copy by the bulk-copy engine, completing on
+// an mbarrier (transaction bytes). Both addresses 16-byte aligned, size a
+// multiple of 16. Plain (non-multicast) form.
+__device__ __forceinline__ void bulk_load_1d(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }

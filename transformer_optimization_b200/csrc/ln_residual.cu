@@ -9,12 +9,16 @@
 // the two-pass moments over the row held in registers, as the reference
 // kernel does (mean first, then the centred sum of squares).
 //
-// Layout: one warp per row (grid-stride over rows), 8 warps per 256-thread
-// block, as many blocks as are resident on the device. Each lane owns
-// 8-element chunks (two float4 of x, one 16-byte vector of fp16 delta) at
-// chunk index lane + 32*i, so every warp-wide load is a contiguous,
-// fully-coalesced 512 B (fp32) or 256 B (fp16) segment. HBM-bound: bytes per
-// row = D*(4 read x + 2 read delta + 4 write x + 2 write normed).
+// HBM-bound: bytes per row = D*(4 read x + 2 read delta + 4 write x + 2 write
+// normed). Two kernels:
+//  * ln_stream_kernel (D <= 2048): one persistent CTA per SM streams groups of
+//    8 rows through a ring of shared-memory stages filled by the bulk-copy
+//    engine (cp.async.bulk, one copy for the 8 x rows and one for the 8 delta
+//    rows of a group), so ~100-200 KB per SM are in flight independent of
+//    registers; two teams of 8 consumer warps take alternate groups, one row
+//    per warp, and store the results straight to HBM.
+//  * ln_residual_kernel (any D up to 4096): one warp per row with the row in
+//    registers, grid-stride over rows.
 #include "common.cuh"
 #include "launch.h"
 
@@ -123,6 +127,156 @@ __global__ void __launch_bounds__(256) ln_residual_kernel(const float* __restric
   }  // row loop
 }
 
+
+// ---------------------------------------------------------------------------
+// Streaming variant: bulk-copy ring of 8-row groups
+// ---------------------------------------------------------------------------
+constexpr int kLnsRows = 8;        // rows per group (one consumer warp each)
+constexpr int kLnsTeams = 2;       // consumer teams working on alternate groups
+constexpr int kLnsThreads = 32 * (kLnsRows * kLnsTeams + 1);  // + 1 producer warp
+constexpr int kLnsMaxStages = 8;
+constexpr int kLnsSmemBudget = 196608;
+
+struct LnsParams {
+  const float* x;
+  const __half* delta;
+  const float* w;
+  const float* b;
+  const uint8_t* valid;
+  float* x_out;
+  void* normed;
+  long long M;
+  int D, flags, stages;
+  float eps;
+  int* status;
+};
+
+template <int NV>  // float4 per lane (row width up to 128*NV)
+__global__ void __launch_bounds__(kLnsThreads, 1) ln_stream_kernel(const LnsParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+  const int D = p.D;
+  const bool has_delta = p.delta != nullptr;
+  const uint32_t x_bytes = static_cast<uint32_t>(kLnsRows) * D * 4;
+  const uint32_t stage_bytes = x_bytes + (has_delta ? static_cast<uint32_t>(kLnsRows) * D * 2 : 0u);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.stages * stage_bytes);
+  uint64_t* empty = full + kLnsMaxStages;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long groups = (p.M + kLnsRows - 1) / kLnsRows;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < p.stages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], kLnsRows);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == kLnsRows * kLnsTeams) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      int it = 0;
+      for (long long g = blockIdx.x; g < groups; g += gridDim.x, ++it) {
+        const int s = it % p.stages;
+        if (!mbar_wait(&empty[s], ((it / p.stages) & 1) ^ 1, p.status, kDevTimeoutProducer)) break;
+        const long long r0 = g * kLnsRows;
+        const int nrows = static_cast<int>(p.M - r0 < kLnsRows ? p.M - r0 : kLnsRows);
+        uint8_t* st = smem + s * stage_bytes;
+        const uint32_t xb = static_cast<uint32_t>(nrows) * D * 4;
+        const uint32_t db = has_delta ? static_cast<uint32_t>(nrows) * D * 2 : 0u;
+        mbar_arrive_expect_tx(&full[s], xb + db);
+        bulk_load_1d(st, p.x + r0 * D, xb, &full[s]);
+        if (has_delta) bulk_load_1d(st + x_bytes, p.delta + r0 * D, db, &full[s]);
+      }
+    }
+    return;
+  }
+
+  // ---------------- consumers ----------------
+  // team k = warp / 8 takes this CTA's groups k, k+2, k+4, ...; warp w of
+  // the team takes row w % 8 of each
+  const int nv = D >> 2;  // float4 per row
+  const int team = warp / kLnsRows, wr = warp % kLnsRows;
+  int it = team;
+  for (long long g = blockIdx.x + static_cast<long long>(team) * gridDim.x; g < groups;
+       g += static_cast<long long>(kLnsTeams) * gridDim.x, it += kLnsTeams) {
+    const int s = it % p.stages;
+    const long long row = g * kLnsRows + wr;
+    const bool have = row < p.M;
+    bool row_valid = true;
+    if (p.valid != nullptr && have) row_valid = p.valid[row] != 0;
+    if (!mbar_wait(&full[s], (it / p.stages) & 1, p.status, kDevTimeoutEpilogue)) break;
+    if (have) {
+      const float4* xs = reinterpret_cast<const float4*>(smem + s * stage_bytes) + static_cast<long long>(wr) * nv;
+      const uint2* ds = reinterpret_cast<const uint2*>(smem + s * stage_bytes + x_bytes) + static_cast<long long>(wr) * nv;
+      const bool keep = !(p.flags & TF_LN_MASK_DELTA) || row_valid;
+      const bool zero_x = (p.flags & TF_LN_MASK_X) && !row_valid;
+      float v[NV][4];
+      float sum = 0.f;
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        const int c = lane + 32 * i;
+        if (c < nv) {
+          const float4 a = xs[c];
+          v[i][0] = a.x; v[i][1] = a.y; v[i][2] = a.z; v[i][3] = a.w;
+          if (has_delta && keep) {
+            const uint2 dq = ds[c];
+            const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&dq.x));
+            const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&dq.y));
+            v[i][0] += f0.x; v[i][1] += f0.y; v[i][2] += f1.x; v[i][3] += f1.y;
+          }
+          if (zero_x) v[i][0] = v[i][1] = v[i][2] = v[i][3] = 0.f;
+          sum += (v[i][0] + v[i][1]) + (v[i][2] + v[i][3]);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);  // the row is in registers
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+      const float mean = sum / static_cast<float>(D);
+      float sq = 0.f;
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        if (lane + 32 * i < nv) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float d = v[i][j] - mean;
+            sq += d * d;
+          }
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+      const float rstd = rsqrtf(sq / static_cast<float>(D) + p.eps);
+      const bool zero_out = (p.flags & TF_LN_MASK_OUT) && !row_valid;
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        const int c = lane + 32 * i;
+        if (c < nv) {
+          if (p.flags & TF_LN_WRITE_X)
+            __stcs(reinterpret_cast<float4*>(p.x_out + row * D) + c, make_float4(v[i][0], v[i][1], v[i][2], v[i][3]));
+          const float4 wv = __ldg(reinterpret_cast<const float4*>(p.w) + c);
+          const float4 bv = __ldg(reinterpret_cast<const float4*>(p.b) + c);
+          float y0 = (v[i][0] - mean) * rstd * wv.x + bv.x;
+          float y1 = (v[i][1] - mean) * rstd * wv.y + bv.y;
+          float y2 = (v[i][2] - mean) * rstd * wv.z + bv.z;
+          float y3 = (v[i][3] - mean) * rstd * wv.w + bv.w;
+          if (zero_out) y0 = y1 = y2 = y3 = 0.f;
+          if (p.flags & TF_LN_OUT_F32) {
+            __stcs(reinterpret_cast<float4*>(static_cast<float*>(p.normed) + row * D) + c, make_float4(y0, y1, y2, y3));
+          } else {
+            __stcs(reinterpret_cast<uint2*>(static_cast<__half*>(p.normed) + row * D) + c,
+                   make_uint2(pack_half2(y0, y1), pack_half2(y2, y3)));
+          }
+        }
+      }
+    } else {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
+  }
+}
+
 int ln_residual(const float* x, const void* delta, const float* w, const float* b, float eps,
                 const uint8_t* valid, long long M, int D, int flags, float* x_out, void* normed,
                 cudaStream_t stream) {
@@ -138,6 +292,55 @@ int ln_residual(const float* x, const void* delta, const float* w, const float* 
   if ((flags & (TF_LN_MASK_DELTA | TF_LN_MASK_X | TF_LN_MASK_OUT)) && valid == nullptr)
     return set_error(TF_ERR_SHAPE, "ln_residual: mask flag without a valid-token mask");
   if (!(flags & (TF_LN_MASK_DELTA | TF_LN_MASK_X | TF_LN_MASK_OUT))) valid = nullptr;
+  if (D <= 2048) {
+    LnsParams lp;
+    lp.x = x;
+    lp.delta = static_cast<const __half*>(delta);
+    lp.w = w;
+    lp.b = b;
+    lp.valid = valid;
+    lp.x_out = x_out;
+    lp.normed = normed;
+    lp.M = M;
+    lp.D = D;
+    lp.flags = flags;
+    lp.eps = eps;
+    lp.status = device_status_ptr();
+    if (lp.status == nullptr) return last_error_code();
+    const int stage_bytes = kLnsRows * D * (delta != nullptr ? 6 : 4);
+    int stages = kLnsSmemBudget / stage_bytes;
+    stages = stages > kLnsMaxStages ? kLnsMaxStages : (stages < 2 ? 2 : stages);
+    lp.stages = stages;
+    const int smem = stages * stage_bytes + 2 * kLnsMaxStages * 8 + 128;
+    const long long groups = (M + kLnsRows - 1) / kLnsRows;
+    const long long grid = groups < device_sm_count() ? groups : device_sm_count();
+    const int nv = (D / 4 + 31) / 32;
+    int dev = 0;
+    cudaGetDevice(&dev);
+#define TFB_LNS_CASE(N)                                                                             \
+  {                                                                                                 \
+    static bool attr_done[64] = {};                                                                 \
+    if (!attr_done[dev & 63]) {                                                                     \
+      cudaError_t ea = cudaFuncSetAttribute(ln_stream_kernel<N>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                                            kLnsSmemBudget + 2 * kLnsMaxStages * 8 + 128);          \
+      if (ea != cudaSuccess)                                                                        \
+        return set_error(TF_ERR_LAUNCH, "cudaFuncSetAttribute(ln): %s", cudaGetErrorString(ea));    \
+      attr_done[dev & 63] = true;                                                                   \
+    }                                                                                               \
+    ln_stream_kernel<N><<<static_cast<unsigned>(grid), kLnsThreads, smem, stream>>>(lp);            \
+  }                                                                                                 \
+  break;
+    switch (nv <= 2 ? 2 : nv <= 4 ? 4 : nv <= 8 ? 8 : 16) {
+      case 2: TFB_LNS_CASE(2)
+      case 4: TFB_LNS_CASE(4)
+      case 8: TFB_LNS_CASE(8)
+      default: TFB_LNS_CASE(16)
+    }
+#undef TFB_LNS_CASE
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return set_error(TF_ERR_LAUNCH, "ln_residual launch: %s", cudaGetErrorString(e));
+    return TF_OK;
+  }
   // grid-stride over rows with the device filled exactly (resident blocks
   // per SM from the occupancy of this instantiation)
   const int nch = (D / 8 + 31) / 32;
