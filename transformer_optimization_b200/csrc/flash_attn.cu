@@ -82,8 +82,8 @@ struct AttnCfg {
   static constexpr int kVOff = kKOff + kKStages * kTileBytes;
   static constexpr int kBarOff = kVOff + kVStages * kTileBytes;
   // q_full, k_full/empty[KS], v_full/empty[VS], s_full[NS],
-  // p_full[2 tiles x 2 alternating], o_full[2], turn[2], drain
-  static constexpr int kNumBars = 1 + 2 * kKStages + 2 * kVStages + kNS + 4 + 2 + 2 + 1;
+  // p_full[2 tiles x 2 alternating], o_full[2], turn[2], drain[2], pv_done[NS]
+  static constexpr int kNumBars = 1 + 2 * kKStages + 2 * kVStages + kNS + 4 + 2 + 2 + 2 + kNS;
   static constexpr int kBytes = kBarOff + kNumBars * 8 + 16;
   static constexpr int kAlloc = kBytes + 1024;
   // TMEM columns: S/P slots at 0, 128, ..; O_t at kNS*128 + t*HD (512 in all)
@@ -212,8 +212,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint64_t* p_full = s_full + NS;  // [tile * 2 + (block & 1)]: alternating, so no waiter falls two phases behind
   uint64_t* o_full = p_full + 4;   // [tile]: every PV of the tile so far has landed in O
   uint64_t* turn = o_full + 2;     // exp-phase hand-off between the two softmax warpgroups
-  uint64_t* drain = turn + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* drain = turn + 2;       // [issuer]: end-of-kernel drain of each MMA issuer
+  uint64_t* pv_done = drain + 2;    // [slot]: the PV that read this slot's P has completed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pv_done + NS);
 
   const int warp = warp_id();
   const int lane = lane_id();
@@ -262,7 +263,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       mbar_init(&o_full[i], 1);
       mbar_init(&turn[i], 128);
     }
-    mbar_init(drain, 1);
+    mbar_init(&drain[0], 1);
+    mbar_init(&drain[1], 1);
+    for (int i = 0; i < NS; ++i) mbar_init(&pv_done[i], 1);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -315,9 +318,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       for (int i = (j > VS ? j - VS : 0); i < j; ++i)
         mbar_wait(&v_full[i % VS], (i / VS) & 1, p.status, kDevTimeoutDrain);
     }
-  } else if (warp == 1) {
+  } else if (warp == 1 || warp == 3) {
     if (lane == 0 && nmax > 0) {
-      // ---------------- MMA issuer ----------------
+      // ---------------- MMA issuers ----------------
+      // Two threads feed the tensor core: warp 1 issues the S = Q K^T
+      // products, warp 3 the O += P V products. Each stream waits only on
+      // its own inputs, so neither stalls behind the other's barrier waits
+      // and commits (the tensor core queue is shallow). A slot's next S
+      // waits for the completion of the PV that read the slot's P (pv_done).
       constexpr uint32_t idesc_s = idesc_f16_f32(kAttnBM, kAttnBN);     // K-major Q, K-major K
       constexpr uint32_t idesc_o = idesc_f16_f32(kAttnBM, HD, false, true);  // K-major P, MN-major V
       const uint32_t sbase = smem_u32(smem);
@@ -332,52 +340,51 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       };
       // the last pair (in issue order) that reads key block j
       auto last_user = [&](int t, int j) { return t == 1 || j >= nblk[1]; };
-      auto issue_s = [&](int q) -> bool {
-        int t, j;
-        pair_of(q, t, j);
-        const int slot = q % NS;
-        // the slot's previous P (pair q - NS) was consumed by a PV issued
-        // before this point, hence executed before these MMAs
-        if (!mbar_wait(&k_full[j % KS], (j / KS) & 1, p.status, kDevTimeoutMma)) return false;
-        tc_fence_after();
-        const uint32_t qa = sbase + C::kQOff + t * C::kTileBytes;
-        const uint32_t ka = sbase + C::kKOff + (j % KS) * C::kTileBytes;
+      bool ok = true;
+      if (warp == 1) {
+        ok = mbar_wait(q_full, 0, p.status, kDevTimeoutMma);
+        for (int q = 0; q < n_pairs && ok; ++q) {
+          int t, j;
+          pair_of(q, t, j);
+          const int slot = q % NS;
+          if (q >= NS && !(ok = mbar_wait(&pv_done[slot], ((q - NS) / NS) & 1, p.status, kDevTimeoutMma))) break;
+          if (!(ok = mbar_wait(&k_full[j % KS], (j / KS) & 1, p.status, kDevTimeoutMma))) break;
+          tc_fence_after();
+          const uint32_t qa = sbase + C::kQOff + t * C::kTileBytes;
+          const uint32_t ka = sbase + C::kKOff + (j % KS) * C::kTileBytes;
 #pragma unroll
-        for (int k = 0; k < HD / 16; ++k) {
-          const uint32_t off = (k >> 2) * 16384 + (k & 3) * 32;
-          umma_f16_ss(tmem_base + C::kTmS + slot * 128, smem_desc_sw128(qa + off, 16, 1024),
-                      smem_desc_sw128(ka + off, 16, 1024), idesc_s, k > 0 ? 1u : 0u);
+          for (int k = 0; k < HD / 16; ++k) {
+            const uint32_t off = (k >> 2) * 16384 + (k & 3) * 32;
+            umma_f16_ss(tmem_base + C::kTmS + slot * 128, smem_desc_sw128(qa + off, 16, 1024),
+                        smem_desc_sw128(ka + off, 16, 1024), idesc_s, k > 0 ? 1u : 0u);
+          }
+          umma_commit(&s_full[slot]);
+          if (last_user(t, j)) umma_commit(&k_empty[j % KS]);
         }
-        umma_commit(&s_full[slot]);
-        if (last_user(t, j)) umma_commit(&k_empty[j % KS]);
-        return true;
-      };
-      auto issue_pv = [&](int q) -> bool {
-        int t, j;
-        pair_of(q, t, j);
-        const int slot = q % NS;
-        if (!mbar_wait(&v_full[j % VS], (j / VS) & 1, p.status, kDevTimeoutMma)) return false;
-        if (!mbar_wait(&p_full[t * 2 + (j & 1)], (j >> 1) & 1, p.status, kDevTimeoutMma)) return false;
-        tc_fence_after();
-        const uint32_t va = sbase + C::kVOff + (j % VS) * C::kTileBytes;
-        // P: 128 keys = 64 TMEM columns, 8 per MMA; V: MN-major, 8-key groups
-        // at 1024 B (SBO), 64-wide head-dim blocks at 16 KB (LBO)
+      } else {
+        for (int q = 0; q < n_pairs && ok; ++q) {
+          int t, j;
+          pair_of(q, t, j);
+          const int slot = q % NS;
+          if (!(ok = mbar_wait(&v_full[j % VS], (j / VS) & 1, p.status, kDevTimeoutMma))) break;
+          if (!(ok = mbar_wait(&p_full[t * 2 + (j & 1)], (j >> 1) & 1, p.status, kDevTimeoutMma))) break;
+          tc_fence_after();
+          const uint32_t va = sbase + C::kVOff + (j % VS) * C::kTileBytes;
+          // P: 128 keys = 64 TMEM columns, 8 per MMA; V: MN-major, 8-key
+          // groups at 1024 B (SBO), 64-wide head-dim blocks at 16 KB (LBO)
 #pragma unroll
-        for (int k = 0; k < kAttnBN / 16; ++k)
-          umma_f16_ts(tmem_base + C::kTmO + t * HD, tmem_base + C::kTmS + slot * 128 + k * 8,
-                      smem_desc_sw128(va + k * 2048, 16384, 1024), idesc_o, (j > 0 || k > 0) ? 1u : 0u);
-        umma_commit(&o_full[t]);
-        if (last_user(t, j)) umma_commit(&v_empty[j % VS]);
-        return true;
-      };
-      bool ok = mbar_wait(q_full, 0, p.status, kDevTimeoutMma);
-      for (int q = 0; q < NS && q < n_pairs && ok; ++q) ok = issue_s(q);
-      for (int q = 0; q < n_pairs && ok; ++q) {
-        ok = issue_pv(q);
-        if (ok && q + NS < n_pairs) ok = issue_s(q + NS);
+          for (int k = 0; k < kAttnBN / 16; ++k)
+            umma_f16_ts(tmem_base + C::kTmO + t * HD, tmem_base + C::kTmS + slot * 128 + k * 8,
+                        smem_desc_sw128(va + k * 2048, 16384, 1024), idesc_o, (j > 0 || k > 0) ? 1u : 0u);
+          umma_commit(&pv_done[slot]);
+          umma_commit(&o_full[t]);
+          if (last_user(t, j)) umma_commit(&v_empty[j % VS]);
+        }
       }
-      umma_commit(drain);
-      mbar_wait(drain, 0, p.status, kDevTimeoutDrain);
+      // drain: every MMA this thread issued completes before TMEM is released
+      uint64_t* d = &drain[warp == 1 ? 0 : 1];
+      umma_commit(d);
+      mbar_wait(d, 0, p.status, kDevTimeoutDrain);
     }
   }
   } else {
