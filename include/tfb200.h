@@ -64,7 +64,7 @@ extern "C" {
                                rounded to fp16 for the PV product either way) */
 /* flags bits 8..15: how many of the 64 probability pairs per row and key
  * block are exponentiated on the FMA pipes instead of the exp unit
- * (0, 16, 24 or 32; packed fp16 exp path only) */
+ * (0, 8, 16 or 24; with TF_ATTN_EXP_F16X2: 0 or 16) */
 #define TF_ATTN_FMA_EXP_SHIFT 8
 
 /* ABI version, bumped on any signature change. */

@@ -269,11 +269,11 @@ def test_flash_packed_qkv(K, b, h, sq, sk, hd, causal, masked, exp_f16x2):
     assert torch.allclose(lse[fin], lse_ref[fin], atol=2e-3, rtol=1e-4)
 
 
-@pytest.mark.parametrize("pairs", [16, 24, 32])
+@pytest.mark.parametrize("pairs,f16x2", [(8, False), (16, False), (24, False), (16, True)])
 @pytest.mark.parametrize("b,h,sq,hd,causal,masked", [(2, 4, 300, 64, True, True), (1, 2, 513, 128, False, False)])
-def test_flash_fma_exp(K, pairs, b, h, sq, hd, causal, masked):
-    """Part of the exponentials on the FMA pipes (binary16 built from a
-    polynomial) gives the same attention within the fp16-P tolerance."""
+def test_flash_fma_exp(K, pairs, f16x2, b, h, sq, hd, causal, masked):
+    """Part of the exponentials on the FMA pipes (fp32 or binary16 built from
+    a polynomial) gives the same attention within the fp16-P tolerance."""
     d = h * hd
     qkv = _qkv(b, h, sq, hd, pairs + sq)
     kv_valid = None
@@ -286,7 +286,7 @@ def test_flash_fma_exp(K, pairs, b, h, sq, hd, causal, masked):
     g = qkv.cuda()
     out, lse = K.flash_attention(g[..., :d], g[..., d:2 * d], g[..., 2 * d:], h, hd ** -0.5, causal=causal,
                                  key_valid=None if kv_valid is None else kv_valid.cuda(), want_lse=True,
-                                 fma_exp_pairs=pairs)
+                                 fma_exp_pairs=pairs, exp_f16x2=f16x2)
     out = out.float().cpu()
     assert torch.all((out - ref).abs() <= 1e-2 * ref.abs() + 3e-3), (out - ref).abs().max()
     fin = torch.isfinite(lse_ref)

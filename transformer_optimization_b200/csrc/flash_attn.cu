@@ -92,9 +92,10 @@ struct AttnCfg {
   static_assert(kNS * 128 + kAttnTiles * HD <= 512, "TMEM budget");
 };
 
+// volatile: the exp-unit sweep must stay between the turn wait and arrive
 __device__ __forceinline__ float ex2_f32(float x) {
   float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  asm volatile("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
 
@@ -115,7 +116,7 @@ __device__ __forceinline__ float fmax3f(float a, float b, float c) {
 
 __device__ __forceinline__ uint32_t ex2_f16x2(uint32_t h) {
   uint32_t r;
-  asm("ex2.approx.f16x2 %0, %1;" : "=r"(r) : "r"(h));
+  asm volatile("ex2.approx.f16x2 %0, %1;" : "=r"(r) : "r"(h));
   return r;
 }
 
@@ -127,6 +128,24 @@ __device__ __forceinline__ uint32_t ex2_f16x2(uint32_t h) {
 // the binary16 pattern (n + 15) * 1024 + round(1024 * 2^f) - 1024, where a
 // mantissa that rounds up to 2048 carries into the exponent field. Results
 // below 2^-14 (fp16 subnormals) flush to zero.
+// 2^t in fp32 on the FMA/integer pipes (not the exp unit), for t <= 8 (t
+// may be -inf): the same reduction and degree-3 polynomial as
+// exp2_f16_bits_fma (relative error <= 8.6e-5, below half an fp16 ulp, which
+// is the precision P is used at), then n added to the exponent field.
+// Results below 2^-126 are 0.
+__device__ __forceinline__ float exp2_f32_fma(float t) {
+  const float kRound = 12582912.0f;  // 1.5 * 2^23
+  const float y = (t - 0.5f) + kRound;
+  const float f = t - (y - kRound);  // in [0, 1]
+  float p = fmaf(f, 0.07706703990697861f, 0.22764499485492706f);
+  p = fmaf(p, f, 0.6951167583465576f);
+  p = fmaf(p, f, 1.0f);
+  // the low 9 bits of bits(y) hold n mod 512 (kRound's are zero), so
+  // bits(y) << 23 is n << 23 mod 2^32
+  const float r = __uint_as_float(__float_as_uint(p) + (__float_as_uint(y) << 23));
+  return t < -126.0f ? 0.f : r;
+}
+
 __device__ __forceinline__ uint32_t exp2_f16_bits_fma(float t) {
   const float kRound = 12582912.0f;  // 1.5 * 2^23: y = x + kRound keeps round(x) in the low bits of y
   const float y = (t - 0.5f) + kRound;
@@ -490,26 +509,35 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
       const float m_use = m_ref == -INFINITY ? 0.f : m_ref;
 
-      // ---- exp phase, in turns with the other tile's warpgroup ----
-      // tile 0 of block j goes after tile 1 of block j-1, tile 1 of block j
-      // after tile 0 of block j, so one group's exponentials overlap the
-      // other group's TMEM load / max / P store.
-      if (j < n_pp && (t == 1 || j > 0)) {
-        const uint32_t par = t == 0 ? ((j - 1) & 1) : (j & 1);
-        if (!(ok = mbar_wait(&turn[t], par, p.status, kDevTimeoutSoftmax))) break;
-      }
-      // three independent sweeps (scale, pack, exponentiate) so the exp
-      // unit streams back to back instead of waiting on each pair's chain
+      // ---- exponentials ----
+      // Only the exp-unit instructions run in turns with the other tile's
+      // warpgroup (tile 0 of block j after tile 1 of block j-1, tile 1 of
+      // block j after tile 0 of block j): the scale/shift and packing before
+      // the turn, the FMA-pipe exponentials, the row sum and the P store
+      // after it, where they overlap the other group's exp-unit sweep.
       uint32_t pk[64];
       float ls[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int i = 0; i < 128; ++i) s[i] = fmaf(s[i], c, -m_use);
       if constexpr (EXP16) {
-        // POLY of the 64 pairs on the FMA pipes, the rest on the exp unit
 #pragma unroll
         for (int i = POLY; i < 64; ++i) pk[i] = pack_f16x2_rn(s[2 * i], s[2 * i + 1]);
+      }
+      if (j < n_pp && (t == 1 || j > 0)) {
+        const uint32_t par = t == 0 ? ((j - 1) & 1) : (j & 1);
+        if (!(ok = mbar_wait(&turn[t], par, p.status, kDevTimeoutSoftmax))) break;
+      }
+      if constexpr (EXP16) {
+        // POLY of the 64 pairs on the FMA pipes, the rest on the exp unit
 #pragma unroll
         for (int i = POLY; i < 64; ++i) pk[i] = ex2_f16x2(pk[i]);
+      } else {
+        // 2*POLY of the 128 on the FMA pipes, the rest on the exp unit
+#pragma unroll
+        for (int i = 2 * POLY; i < 128; ++i) s[i] = ex2_f32(s[i]);
+      }
+      if (j < n_pp) mbar_arrive(&turn[1 - t]);
+      if constexpr (EXP16) {
 #pragma unroll
         for (int i = 0; i < POLY; ++i)
           pk[i] = exp2_f16_bits_fma(s[2 * i]) | (exp2_f16_bits_fma(s[2 * i + 1]) << 16);
@@ -520,7 +548,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         }
       } else {
 #pragma unroll
-        for (int i = 0; i < 128; ++i) s[i] = ex2_f32(s[i]);
+        for (int i = 0; i < 2 * POLY; ++i) s[i] = exp2_f32_fma(s[i]);
 #pragma unroll
         for (int i = 0; i < 64; ++i) {
           pk[i] = pack_f16x2_rn(s[2 * i], s[2 * i + 1]);
@@ -528,7 +556,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         }
       }
       l += ((ls[0] + ls[1]) + (ls[2] + ls[3])) + ((ls[4] + ls[5]) + (ls[6] + ls[7]));
-      if (j < n_pp) mbar_arrive(&turn[1 - t]);
 
       // P into the first 64 columns of this pair's S slot (already read)
       tmem_st64(tm_s + slot * 128, pk);
@@ -700,25 +727,27 @@ int flash_fwd(const AttnArgs& a, cudaStream_t stream) {
   if (kp.status == nullptr) return last_error_code();
   dim3 grid(kp.q_blocks, static_cast<unsigned>(a.heads), static_cast<unsigned>(a.batch));
   const bool exp16 = (a.flags & TF_ATTN_EXP_F16X2) != 0;
-  // pairs per row whose exponentials run on the FMA pipes (flags bits 8..15)
+  // probability pairs per row and key block whose exponentials run on the
+  // FMA pipes instead of the exp unit (flags bits 8..15)
   const int poly = (a.flags >> 8) & 0xFF;
-  if (poly != 0 && poly != 16 && poly != 24 && poly != 32)
-    return set_error(TF_ERR_SHAPE, "flash: FMA-pipe exp pairs must be 0, 16, 24 or 32");
-  if (poly != 0 && !exp16) return set_error(TF_ERR_SHAPE, "flash: FMA-pipe exp pairs need TF_ATTN_EXP_F16X2");
-  if (!exp16) {
-    return a.head_dim == 64 ? launch_flash<64, false, 0>(tq, tk, tv, kp, grid, stream)
-                            : launch_flash<128, false, 0>(tq, tk, tv, kp, grid, stream);
+  if (poly != 0 && poly != 8 && poly != 16 && poly != 24)
+    return set_error(TF_ERR_SHAPE, "flash: FMA-pipe exp pairs must be 0, 8, 16 or 24");
+  if (exp16 && poly != 0 && poly != 16)
+    return set_error(TF_ERR_SHAPE, "flash: with TF_ATTN_EXP_F16X2 the FMA-pipe exp pairs must be 0 or 16");
+#define TFB_FLASH(E, P)                                                            \
+  return a.head_dim == 64 ? launch_flash<64, E, P>(tq, tk, tv, kp, grid, stream) \
+                          : launch_flash<128, E, P>(tq, tk, tv, kp, grid, stream);
+  if (exp16) {
+    if (poly == 16) TFB_FLASH(true, 16)
+    TFB_FLASH(true, 0)
   }
-#define TFB_FLASH_POLY(P)                                                          \
-  return a.head_dim == 64 ? launch_flash<64, true, P>(tq, tk, tv, kp, grid, stream) \
-                          : launch_flash<128, true, P>(tq, tk, tv, kp, grid, stream);
   switch (poly) {
-    case 16: TFB_FLASH_POLY(16)
-    case 24: TFB_FLASH_POLY(24)
-    case 32: TFB_FLASH_POLY(32)
-    default: TFB_FLASH_POLY(0)
+    case 8: TFB_FLASH(false, 8)
+    case 16: TFB_FLASH(false, 16)
+    case 24: TFB_FLASH(false, 24)
+    default: TFB_FLASH(false, 0)
   }
-#undef TFB_FLASH_POLY
+#undef TFB_FLASH
 }
 
 int attn_merge(const MergeArgs& a, cudaStream_t stream) {

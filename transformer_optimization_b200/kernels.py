@@ -185,7 +185,7 @@ def flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, heads: in
             raise ValueError("flash_attention: key_valid must be bool [B, Sk]")
         key_valid = key_valid.contiguous()
     flags = (_abi.TF_ATTN_CAUSAL if causal else 0) | (_abi.TF_ATTN_OUT_F32 if out_dtype == torch.float32 else 0)
-    if exp_f16x2 or fma_exp_pairs:
+    if exp_f16x2:
         flags |= _abi.TF_ATTN_EXP_F16X2
     flags |= (int(fma_exp_pairs) & 0xFF) << 8
     _abi.call("tf_flash_fwd", _ptr(q), _ptr(k), _ptr(v), q.stride(1), k.stride(1), q.stride(0), k.stride(0),
