@@ -42,6 +42,10 @@ from transformer_optimization_b200 import NAMED_CONFIGS, UserOptimizedTransforme
 from transformer_optimization_b200 import kernels as K  # noqa: E402
 
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+# DRAM bytes (read + write) per projection launch of the c3 forward, mean of
+# the four projections of a layer, from one ncu capture of each shape
+# (profiles/gemm_c3_projections.md)
+C3_GEMM_DRAM_BYTES_PER_LAUNCH = 147.9e6
 L2_FLUSH_BYTES = 256 << 20
 
 
@@ -54,6 +58,18 @@ def load_peaks():
         except Exception:
             pass
     return dict(FALLBACK_PEAKS), "fallback"
+
+
+def algo_bytes_per_gemm(cfg):
+    """Mean algorithmic HBM bytes of the four projections of one layer:
+    fp16 A and W read, fp16 C written (QKV, FFN in), or fp32 x read and
+    written around the product (the two residual projections)."""
+    m, d, f = cfg.batch_size * cfg.seq_len, cfg.d_model, cfg.ffn_dim
+    qkv = 2 * (m * d + 3 * d * d + 3 * m * d)
+    ffn_in = 2 * (m * d + f * d + m * f)
+    out_proj = 2 * (m * d + d * d) + 8 * m * d
+    ffn_out = 2 * (m * f + d * f) + 8 * m * d
+    return (qkv + ffn_in + out_proj + ffn_out) / 4
 
 
 def cfg_dict(cfg):
@@ -323,6 +339,8 @@ def run_ours(args, cfg, rank, world, local_rank):
     prof = kernel_profile(model, x)
     flops = count_dense_flops(cfg)
     tensor_peak = peaks["bf16_tflops"]
+    # kernels timed inside a long step run at the sustained (power-capped) clock
+    sustained = peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"])
     n_g, ms_g, fl_g = prof["gemm"]
     n_f, ms_f, fl_f = prof["flash"]
     n_l, ms_l, by_l = prof["ln"]
@@ -344,12 +362,15 @@ def run_ours(args, cfg, rank, world, local_rank):
                 "d2h_bytes_per_step": y_host.numel() * 4, "ms_per_step": e_total / args.steps},
         "gpu_launches": launches_per_step * args.steps,
         "roofline": {"bound": "tensor", "kernel": "gemm_f16_tcgen05", "achieved": gemm_tflops,
-                     "peak": tensor_peak, "unit": "TFLOP/s", "frac": gemm_tflops / tensor_peak,
-                     "peak_source": f"bf16_tflops burst ({peak_src})", "traffic": None,
+                     "peak": sustained, "unit": "TFLOP/s", "frac": gemm_tflops / sustained,
+                     "peak_source": f"bf16_tflops_sustained ({peak_src}): the GEMMs are timed inside the step",
+                     "traffic": C3_GEMM_DRAM_BYTES_PER_LAUNCH if args.config == "c3" else None,
+                     "traffic_unit": "bytes per launch (ncu dram read+write)",
+                     "algorithmic_bytes_per_launch": algo_bytes_per_gemm(cfg),
                      "launches_per_step": n_g, "gemm_share_of_step": ms_g / ms_per_step},
         "kernels": {
             "flash_fwd_tcgen05": {"launches": n_f, "ms": ms_f, "tflops": flash_tflops,
-                                  "frac": flash_tflops / tensor_peak},
+                                  "frac": flash_tflops / sustained},
             "ln_residual": {"launches": n_l, "ms": ms_l, "gbs": ln_gbs, "frac": ln_gbs / peaks["hbm_gbs"]},
             "gemm_f16_tcgen05": {"launches": n_g, "ms": ms_g, "tflops": gemm_tflops},
         },
