@@ -204,6 +204,10 @@ def kernel_profile(model, x):
             torch.cuda.synchronize()
             for lst in rec.values():
                 lst.clear()
+            # hold the GPU for ~0.1 s so the host enqueues the whole forward
+            # ahead of it: the launches then run back to back and each event
+            # pair brackets device time only, not the host's launch latency
+            torch.cuda._sleep(200_000_000)
             model(x)
         torch.cuda.synchronize()
     finally:

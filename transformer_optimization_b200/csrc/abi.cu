@@ -8,6 +8,8 @@
 
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
+
 #include "launch.h"
 
 namespace tfb {
@@ -95,6 +97,14 @@ int set_error(int code, const char* fmt, ...) {
 }
 
 int last_error_code() { return g_code == TF_OK ? TF_ERR_DEVICE : g_code; }
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("TFB_PDL");
+    return !(e != nullptr && e[0] == '0');
+  }();
+  return on;
+}
 
 int device_sm_count() {
   DeviceInfo* di = device_info();

@@ -142,6 +142,12 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
 
 // Generic-proxy writes to shared memory -> visible to the async proxy
 // (tcgen05.mma operand reads).
+// Programmatic dependent launch: wait until the previous kernel on the
+// stream has completed and its writes are visible (no-op when the launch
+// had no programmatic dependency), and allow the next kernel to launch.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // Contiguous global -> shared copy by the bulk-copy engine, completing on
 // an mbarrier (transaction bytes). Both addresses 16-byte aligned, size a
 // multiple of 16. Plain (non-multicast) form.

@@ -295,6 +295,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // everything above touched only this CTA's shared memory and TMEM
+  pdl_wait();
+  pdl_trigger();
   if (warp < 4) {
   asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsLow));
   if (warp == 0) {
@@ -627,6 +630,8 @@ __global__ void attn_merge_kernel(float* __restrict__ o_acc, float* __restrict__
                                   const float* __restrict__ o_part, const float* __restrict__ lse_part,
                                   long long ld, long long bs, __half* __restrict__ out16, long long ld16,
                                   long long bs16, int heads, int seq_q, int hd) {
+  pdl_wait();
+  pdl_trigger();
   // one warp per (b, h, row); lanes stride over head_dim
   const long long gw = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
@@ -676,8 +681,7 @@ static int launch_flash(const CUtensorMap& tq, const CUtensorMap& tk, const CUte
     if (e != cudaSuccess) return set_error(TF_ERR_LAUNCH, "cudaFuncSetAttribute(flash): %s", cudaGetErrorString(e));
     attr_done[dev & 63] = true;
   }
-  kern<<<grid, kAttnThreads, C::kAlloc, stream>>>(tq, tk, tv, kp);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_k(kern, grid, dim3(kAttnThreads), C::kAlloc, stream, tq, tk, tv, kp);
   if (e != cudaSuccess) return set_error(TF_ERR_LAUNCH, "flash launch: %s", cudaGetErrorString(e));
   return TF_OK;
 }
@@ -759,10 +763,9 @@ int attn_merge(const MergeArgs& a, cudaStream_t stream) {
   const long long blocks = (warps * 32 + 255) / 256;
   if (blocks > 0x7fffffffll) return set_error(TF_ERR_SHAPE, "merge: too many rows");
   dim3 grid(static_cast<unsigned>(blocks), static_cast<unsigned>(a.batch));
-  attn_merge_kernel<<<grid, 256, 0, stream>>>(a.o_acc, a.lse_acc, a.o_part, a.lse_part, a.ld, a.bs,
-                                              static_cast<__half*>(a.out16), a.ld16, a.bs16,
-                                              static_cast<int>(a.heads), static_cast<int>(a.seq_q),
-                                              static_cast<int>(a.head_dim));
+  launch_k(attn_merge_kernel, grid, dim3(256), 0, stream, a.o_acc, a.lse_acc, a.o_part, a.lse_part, a.ld, a.bs,
+           static_cast<__half*>(a.out16), a.ld16, a.bs16, static_cast<int>(a.heads), static_cast<int>(a.seq_q),
+           static_cast<int>(a.head_dim));
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(TF_ERR_LAUNCH, "merge launch: %s", cudaGetErrorString(e));
   return TF_OK;

@@ -163,6 +163,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // everything above touched only this CTA's shared memory and TMEM
+  pdl_wait();
+  pdl_trigger();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -353,6 +356,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemm2Threads, 1)
   cluster_sync_all();  // barriers of both CTAs initialised before any remote arrive
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // everything above touched only this CTA's shared memory and TMEM
+  pdl_wait();
+  pdl_trigger();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -493,8 +499,7 @@ static int launch_gemm_cfg(const CUtensorMap& ta, const CUtensorMap& tb, const G
     if (e != cudaSuccess) return set_error(TF_ERR_LAUNCH, "cudaFuncSetAttribute(gemm): %s", cudaGetErrorString(e));
     attr_done[dev & 63] = true;
   }
-  kern<<<grid, kGemmThreads, L::kAlloc, stream>>>(ta, tb, args);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_k(kern, dim3(grid), dim3(kGemmThreads), L::kAlloc, stream, ta, tb, args);
   if (e != cudaSuccess) return set_error(TF_ERR_LAUNCH, "gemm launch: %s", cudaGetErrorString(e));
   return TF_OK;
 }
@@ -512,8 +517,7 @@ static int launch_gemm2_cfg(const CUtensorMap& ta, const CUtensorMap& tb, const 
     if (e != cudaSuccess) return set_error(TF_ERR_LAUNCH, "cudaFuncSetAttribute(gemm2): %s", cudaGetErrorString(e));
     attr_done[dev & 63] = true;
   }
-  kern<<<grid, kGemm2Threads, L::kAlloc, stream>>>(ta, tb, args);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_k(kern, dim3(grid), dim3(kGemm2Threads), L::kAlloc, stream, ta, tb, args);
   if (e != cudaSuccess) return set_error(TF_ERR_LAUNCH, "gemm2 launch: %s", cudaGetErrorString(e));
   return TF_OK;
 }

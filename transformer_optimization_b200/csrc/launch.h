@@ -6,6 +6,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "../../include/tfb200.h"
 
 namespace tfb {
@@ -32,6 +34,30 @@ int make_tmap_2d_f16(CUtensorMap* map, const void* base, long long inner, long l
 // pitch `bstride` (elements), 128-byte swizzle, box box_inner x box_rows x 1.
 int make_tmap_3d_f16(CUtensorMap* map, const void* base, long long inner, long long rows, long long batches,
                      long long ld, long long bstride, int box_inner, int box_rows);
+
+// Programmatic dependent launch. Every kernel of this library is launched
+// with programmatic stream serialization: it may start (barrier set-up,
+// TMEM allocation, tensor-map prefetch) while the previous kernel on the
+// stream drains, and waits (griddepcontrol.wait) before it touches global
+// memory the previous kernel may write or read. TFB_PDL=0 in the environment
+// turns it off (plain stream order).
+bool pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                     Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
 
 // kernels (defined in their own translation units)
 struct GemmCall {

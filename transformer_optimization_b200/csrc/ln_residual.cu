@@ -34,6 +34,8 @@ __global__ void __launch_bounds__(256) ln_residual_kernel(const float* __restric
                                                           const uint8_t* __restrict__ valid, long long M, int D,
                                                           int flags, float* __restrict__ x_out,
                                                           void* __restrict__ normed) {
+  pdl_wait();
+  pdl_trigger();
   const int lane = threadIdx.x & 31;
   const long long warps_total = static_cast<long long>(gridDim.x) * kLnRowsPerBlock;
   for (long long row = static_cast<long long>(blockIdx.x) * kLnRowsPerBlock + (threadIdx.x >> 5); row < M;
@@ -171,6 +173,8 @@ __global__ void __launch_bounds__(kLnsThreads, 1) ln_stream_kernel(const LnsPara
     fence_mbar_init();
   }
   __syncthreads();
+  pdl_wait();
+  pdl_trigger();
 
   if (warp == kLnsRows * kLnsTeams) {
     // ---------------- producer ----------------
@@ -327,7 +331,7 @@ int ln_residual(const float* x, const void* delta, const float* w, const float* 
         return set_error(TF_ERR_LAUNCH, "cudaFuncSetAttribute(ln): %s", cudaGetErrorString(ea));    \
       attr_done[dev & 63] = true;                                                                   \
     }                                                                                               \
-    ln_stream_kernel<N><<<static_cast<unsigned>(grid), kLnsThreads, smem, stream>>>(lp);            \
+    launch_k(ln_stream_kernel<N>, dim3(static_cast<unsigned>(grid)), dim3(kLnsThreads), smem, stream, lp); \
   }                                                                                                 \
   break;
     switch (nv <= 2 ? 2 : nv <= 4 ? 4 : nv <= 8 ? 8 : 16) {
@@ -352,8 +356,8 @@ int ln_residual(const float* x, const void* delta, const float* w, const float* 
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, ln_residual_kernel<N>, 256, 0);                    \
     long long blocks = static_cast<long long>(device_sm_count()) * (per_sm > 0 ? per_sm : 1);                 \
     if (blocks > need) blocks = need;                                                                         \
-    ln_residual_kernel<N><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(x, dh, w, b, eps, valid, M, D,   \
-                                                                             flags, x_out, normed);           \
+    launch_k(ln_residual_kernel<N>, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, stream, x, dh, w, b, eps, \
+             valid, M, D, flags, x_out, normed);                                                             \
   }                                                                                                           \
   break;
   switch (nch <= 1 ? 1 : nch <= 2 ? 2 : nch <= 4 ? 4 : nch <= 8 ? 8 : 16) {
