@@ -120,6 +120,26 @@ int tf_gemm_residual(const void* A, int64_t lda, const void* W, int64_t ldw, con
                      const float* x_in, float* x_out, int64_t ldx, const uint8_t* valid, int mask_mode,
                      int64_t M, int64_t N, int64_t K, int w_split, int tile_n, int pair, void* stream);
 
+/* Split-K forms of tf_gemm / tf_gemm_residual for few-row inputs (small
+ * batch x sequence), where 128-row tiles leave most SMs idle: each tile's
+ * K range is cut into `splits` parts (splits <= 0: automatic, about one work
+ * unit per SM); every part writes its fp32 partial product into `workspace`,
+ * and a second kernel sums the parts in a fixed order (deterministic), adds
+ * the bias and applies the same epilogue as the unsplit call. `workspace`:
+ * device memory of at least tf_gemm_splitk_workspace(M, N, K, splits)
+ * bytes, 16-byte aligned, owned by the caller; calls on one workspace must
+ * not overlap in time. No split weights (w_split). Same projections as
+ * tf_gemm / tf_gemm_residual (torch_transformer_benchmark.py:4138-4194;
+ * residual add 3988-3995). */
+int64_t tf_gemm_splitk_workspace(int64_t M, int64_t N, int64_t K, int splits);
+int tf_gemm_splitk(const void* A, int64_t lda, const void* W, int64_t ldw, const float* bias, void* C, int64_t ldc,
+                   int64_t M, int64_t N, int64_t K, int epilogue, int splits, void* workspace,
+                   int64_t workspace_bytes, void* stream);
+int tf_gemm_residual_splitk(const void* A, int64_t lda, const void* W, int64_t ldw, const float* bias,
+                            const float* x_in, float* x_out, int64_t ldx, const uint8_t* valid, int mask_mode,
+                            int64_t M, int64_t N, int64_t K, int splits, void* workspace, int64_t workspace_bytes,
+                            void* stream);
+
 /* Flash attention forward (online softmax, no score matrix in HBM):
  *   out[b, i, h*hd:(h+1)*hd] = sum_j softmax_j(scale * q_i . k_j) v_j
  * q: fp16, token i of batch b, head h at q + b*bs_q + i*ld_q + h*hd;

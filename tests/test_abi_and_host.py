@@ -31,7 +31,7 @@ def _declared():
     text = HEADER.read_text()
     text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
     out = {}
-    for m in re.finditer(r"\b(?:int|const char\s*\*)\s*(tf_\w+)\s*\(([^)]*)\)\s*;", text):
+    for m in re.finditer(r"\b(?:int64_t|int|const char\s*\*)\s*(tf_\w+)\s*\(([^)]*)\)\s*;", text):
         args = [a for a in m.group(2).split(",") if a.strip() and a.strip() != "void"]
         out[m.group(1)] = len(args)
     return out
@@ -57,7 +57,7 @@ def test_header_symbols_exported(lib):
 
 
 def test_abi_version_and_error_string(lib):
-    assert lib.tf_abi_version() == 5
+    assert lib.tf_abi_version() == 6
     assert isinstance(lib.tf_last_error(), bytes)
 
 

@@ -124,6 +124,57 @@ def test_gemm_gelu_accuracy(K):
     assert torch.all(diff <= ulp + 1e-6), f"max diff {diff.max()} at x={xs[diff.argmax()]}"
 
 
+SPLITK_SHAPES = [(64, 512, 1536), (64, 2048, 512), (256, 1024, 256), (300, 1024, 3072), (17, 4096, 64),
+                 (129, 520, 96)]
+
+
+@pytest.mark.parametrize("m,k,n", SPLITK_SHAPES)
+@pytest.mark.parametrize("gelu", [False, True])
+@pytest.mark.parametrize("splits", [0, 1, 3, 7])
+def test_gemm_splitk(K, m, k, n, gelu, splits):
+    """Split-K form (partials in a workspace, fixed-order reduce) against the
+    exact sum; the same call twice is bit-identical."""
+    a, w, bias = _gemm_inputs(m, k, n, m + 3 * k + n + splits)
+    w16 = w.half()
+    ref = om.linear_fp16(a, w16, bias, gelu)
+    ag, wg, bg = a.cuda(), w16.cuda(), bias.cuda()
+    ws = torch.empty(K.splitk_workspace_bytes(m, n, k, splits), dtype=torch.uint8, device="cuda")
+    out = K.linear(ag, wg, bg, gelu=gelu, splits=splits, workspace=ws)
+    again = K.linear(ag, wg, bg, gelu=gelu, splits=splits, workspace=ws)
+    err = (out.float().cpu() - ref).abs()
+    assert torch.all(err <= 2e-3 * ref.abs() + 1e-3), f"max err {err.max()}"
+    assert torch.equal(out, again)
+
+
+@pytest.mark.parametrize("mode", ["none", "mask_delta", "mask_x"])
+@pytest.mark.parametrize("m,k,n", [(64, 2048, 512), (256, 1024, 256), (1000, 512, 1024)])
+def test_gemm_residual_splitk(K, mode, m, k, n):
+    a, w, bias = _gemm_inputs(m, k, n, 5 * m + k)
+    w16 = w.half()
+    g = torch.Generator().manual_seed(m)
+    x = torch.randn(m, n, generator=g)
+    valid = torch.rand(m, generator=g) > 0.2
+    md, mx = mode == "mask_delta", mode == "mask_x"
+    ref = om.linear_residual(a, w16, bias, x, valid, md, mx)
+    out = K.linear_residual(a.cuda(), w16.cuda(), bias.cuda(), x.cuda(), None, valid.cuda(), mask_delta=md,
+                            mask_x=mx, splits=0)
+    assert torch.allclose(out.cpu(), ref, atol=1e-4, rtol=1e-5)
+
+
+def test_gemm_splitk_workspace_checks(K):
+    from transformer_optimization_b200 import _abi
+    a, w, bias = _gemm_inputs(64, 1024, 256, 1)
+    need = K.splitk_workspace_bytes(64, 256, 1024, 4)
+    assert need == 4 * 64 * 256 * 4
+    small = torch.empty(need - 16, dtype=torch.uint8, device="cuda")
+    with pytest.raises(ValueError):
+        K.linear(a.cuda(), w.half().cuda(), bias.cuda(), splits=4, workspace=small)
+    with pytest.raises(_abi.TfError):  # the library's own check
+        _abi.call("tf_gemm_splitk", a.cuda().data_ptr(), 1024, w.half().cuda().data_ptr(), 1024,
+                  bias.cuda().data_ptr(), torch.empty(64, 256, dtype=torch.float16, device="cuda").data_ptr(), 256,
+                  64, 256, 1024, 0, 4, small.data_ptr(), small.numel(), 0)
+
+
 @pytest.mark.parametrize("tile_n", [64, 128, 256])
 def test_gemm_tiles(K, tile_n):
     m, k, n = 777, 1024, 1536

@@ -59,6 +59,10 @@ SIGNATURES = {
     "tf_flash_fwd": ([_P, _P, _P, _I64, _I64, _I64, _I64, _P, _I64, _I64, _P, _P,
                       _I64, _I64, _I64, _I64, _I64, _F, _I64, _I64, _I, _P], _I),
     "tf_attn_merge": ([_P, _P, _P, _P, _I64, _I64, _P, _I64, _I64, _I64, _I64, _I64, _I64, _P], _I),
+    "tf_gemm_splitk_workspace": ([_I64, _I64, _I64, _I], _I64),
+    "tf_gemm_splitk": ([_P, _I64, _P, _I64, _P, _P, _I64, _I64, _I64, _I64, _I, _I, _P, _I64, _P], _I),
+    "tf_gemm_residual_splitk": ([_P, _I64, _P, _I64, _P, _P, _P, _I64, _P, _I, _I64, _I64, _I64, _I, _P, _I64, _P],
+                                _I),
 }
 
 _lib: Optional[ctypes.CDLL] = None
@@ -101,6 +105,14 @@ def check(fn: str, rc: int) -> None:
 def call(fn: str, *args) -> None:
     """Call an ABI function and raise TfError on a non-zero status."""
     check(fn, getattr(load(), fn)(*args))
+
+
+def call_value(fn: str, *args) -> int:
+    """Call an ABI function that returns a value (negative = error)."""
+    v = getattr(load(), fn)(*args)
+    if v < 0:
+        raise TfError(fn, -1, load().tf_last_error().decode())
+    return v
 
 
 def device_status(stream: int = 0) -> int:

@@ -166,7 +166,7 @@ static inline int begin_call() {
 
 extern "C" {
 
-int tf_abi_version(void) { return 5; }
+int tf_abi_version(void) { return 6; }
 
 const char* tf_last_error(void) { return tfb::g_msg; }
 
@@ -266,6 +266,60 @@ int tf_gemm_residual(const void* A, int64_t lda, const void* W, int64_t ldw, con
   g.tile_n = tile_n;
   g.pair = pair;
   return tfb::gemm_f16(g, as_stream(stream));
+}
+
+int64_t tf_gemm_splitk_workspace(int64_t M, int64_t N, int64_t K, int splits) {
+  if (begin_call()) return -1;
+  return tfb::gemm_splitk_workspace_bytes(M, N, K, splits);
+}
+
+int tf_gemm_splitk(const void* A, int64_t lda, const void* W, int64_t ldw, const float* bias, void* C, int64_t ldc,
+                   int64_t M, int64_t N, int64_t K, int epilogue, int splits, void* workspace,
+                   int64_t workspace_bytes, void* stream) {
+  int rc = begin_call();
+  if (rc) return rc;
+  if (epilogue != TF_EPI_BIAS && epilogue != TF_EPI_BIAS_GELU)
+    return set_error(TF_ERR_SHAPE, "tf_gemm_splitk: epilogue=%d (TF_EPI_BIAS or TF_EPI_BIAS_GELU)", epilogue);
+  tfb::GemmCall g = {};
+  g.A = A;
+  g.lda = lda;
+  g.W = W;
+  g.ldw = ldw;
+  g.bias = bias;
+  g.C = C;
+  g.ldc = ldc;
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.epilogue = epilogue;
+  g.a_repeat = 1;
+  return tfb::gemm_splitk_f16(g, splits, static_cast<float*>(workspace), workspace_bytes, as_stream(stream));
+}
+
+int tf_gemm_residual_splitk(const void* A, int64_t lda, const void* W, int64_t ldw, const float* bias,
+                            const float* x_in, float* x_out, int64_t ldx, const uint8_t* valid, int mask_mode,
+                            int64_t M, int64_t N, int64_t K, int splits, void* workspace, int64_t workspace_bytes,
+                            void* stream) {
+  int rc = begin_call();
+  if (rc) return rc;
+  if (mask_mode < 0 || mask_mode > 2) return set_error(TF_ERR_SHAPE, "tf_gemm_residual_splitk: mask_mode=%d", mask_mode);
+  tfb::GemmCall g = {};
+  g.A = A;
+  g.lda = lda;
+  g.W = W;
+  g.ldw = ldw;
+  g.bias = bias;
+  g.x_in = x_in;
+  g.x_out = x_out;
+  g.ldx = ldx;
+  g.valid = valid;
+  g.mask_mode = mask_mode;
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.epilogue = 2;
+  g.a_repeat = 1;
+  return tfb::gemm_splitk_f16(g, splits, static_cast<float*>(workspace), workspace_bytes, as_stream(stream));
 }
 
 int tf_flash_fwd(const void* q, const void* k, const void* v, int64_t ld_q, int64_t ld_kv, int64_t bs_q,

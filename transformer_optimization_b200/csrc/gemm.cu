@@ -34,6 +34,7 @@ constexpr int kGemmBM = 128;
 constexpr int kGemmBK = 64;  // one 128-byte swizzle row of fp16
 constexpr int kGemmThreads = 192;
 constexpr int kEpiTileFloats = 32 * 33;  // one warp's epilogue staging tile
+constexpr int kMaxSplits = 32;           // split-K: most k ranges per tile
 
 struct GemmArgs {
   const float* bias;
@@ -48,6 +49,11 @@ struct GemmArgs {
   int a_repeat;   // 1, or 2 for split weights (W has a_repeat*K columns)
   int m_tiles, n_tiles;
   int* status;
+  // split-K (EPI 3): each tile's k-blocks are cut into `splits` ranges of
+  // kb_per_split; work unit u = tile * splits + split; the fp32 partial of a
+  // unit goes to ws[split][M][N]. splits = 1 otherwise.
+  int splits, kb_per_split;
+  float* ws;
 };
 
 template <int BN, int STAGES>
@@ -84,7 +90,7 @@ __device__ __forceinline__ void load_residual(const GemmArgs& p, float4 (&xv)[8]
 
 template <int EPI>
 __device__ __forceinline__ void epilogue_chunk(const GemmArgs& p, const uint32_t (&r)[32], float* buf, int row0,
-                                               int col0, const float4 (&xv)[8]) {
+                                               int col0, const float4 (&xv)[8], int split = 0) {
   const int lane = threadIdx.x & 31;
 #pragma unroll
   for (int i = 0; i < 32; ++i) buf[lane * 33 + i] = __uint_as_float(r[i]);
@@ -96,6 +102,13 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& p, const uint32_t
     const int rl = it * 4 + (lane >> 3);
     const int row = row0 + rl;
     const float* src = buf + rl * 33 + c4;
+    if constexpr (EPI == 3) {
+      // split-K partial: the raw fp32 sum of this unit's k-blocks (no bias)
+      if (row < p.M)
+        *reinterpret_cast<float4*>(p.ws + (static_cast<long long>(split) * p.M + row) * p.N + col0 + c4) =
+            make_float4(src[0], src[1], src[2], src[3]);
+      continue;
+    }
     float v0 = src[0] + bq.x, v1 = src[1] + bq.y, v2 = src[2] + bq.z, v3 = src[3] + bq.w;
     if (row < p.M) {
       if constexpr (EPI == 2) {
@@ -140,6 +153,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int total_tiles = p.m_tiles * p.n_tiles;
   const int a_blocks = (p.K + kGemmBK - 1) / kGemmBK;
   const int k_blocks = a_blocks * p.a_repeat;
+  // work units: (tile, split) with the k-block range [kb_lo, kb_hi)
+  const int total_units = total_tiles * p.splits;
+  auto unit_range = [&](int u, int& tile, int& sp, int& kb_lo, int& kb_hi) {
+    tile = u / p.splits;
+    sp = u - tile * p.splits;
+    kb_lo = sp * p.kb_per_split;
+    kb_hi = kb_lo + p.kb_per_split < k_blocks ? kb_lo + p.kb_per_split : k_blocks;
+  };
 
   if (warp == 0 && lane == 0) {
     tma_prefetch_map(&tmA);
@@ -172,10 +193,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       // ---------------- TMA producer ----------------
       int it = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+      for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
+        int t, sp, kb_lo, kb_hi;
+        unit_range(u, t, sp, kb_lo, kb_hi);
         const int m0 = (t / p.n_tiles) * kGemmBM;
         const int n0 = (t % p.n_tiles) * BN;
-        for (int kb = 0; kb < k_blocks; ++kb, ++it) {
+        for (int kb = kb_lo; kb < kb_hi; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
           if (!mbar_wait(&empty[s], ph ^ 1, p.status, kDevTimeoutProducer)) {
@@ -204,13 +227,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int it = 0;
       int tc = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x, ++tc) {
+      for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x, ++tc) {
+        int t, sp, kb_lo, kb_hi;
+        unit_range(u, t, sp, kb_lo, kb_hi);
         const int a = tc & 1;
         const uint32_t aph = (tc >> 1) & 1;
         if (!mbar_wait(&tempty[a], aph ^ 1, p.status, kDevTimeoutMma)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + a * BN;
-        for (int kb = 0; kb < k_blocks; ++kb, ++it) {
+        for (int kb = kb_lo; kb < kb_hi; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
           if (!mbar_wait(&full[s], ph, p.status, kDevTimeoutMma)) {
@@ -224,7 +249,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           for (int k = 0; k < kGemmBK / 16; ++k) {
             const uint64_t ad = smem_desc_sw128(sa + k * 32, 16, 1024);
             const uint64_t bd = smem_desc_sw128(sb + k * 32, 16, 1024);
-            umma_f16_ss(d_tmem, ad, bd, idesc, (kb | k) != 0 ? 1u : 0u);
+            umma_f16_ss(d_tmem, ad, bd, idesc, (kb != kb_lo || k != 0) ? 1u : 0u);
           }
           umma_commit(&empty[s]);
         }
@@ -239,7 +264,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
     float* ebuf = reinterpret_cast<float*>(smem + L::kEpiOffset) + (warp - 2) * kEpiTileFloats;
     int tc = 0;
-    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++tc) {
+    for (int u = blockIdx.x; u < total_units; u += gridDim.x, ++tc) {
+      int t, sp, kb_lo, kb_hi;
+      unit_range(u, t, sp, kb_lo, kb_hi);
       const int m0 = (t / p.n_tiles) * kGemmBM;
       const int n0 = (t % p.n_tiles) * BN;
       const int a = tc & 1;
@@ -272,7 +299,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           mbar_arrive(&tempty[a]);
         }
         const int col0 = n0 + c * 32;
-        if (col0 < p.N && row0 < p.M) epilogue_chunk<EPI>(p, cur, ebuf, row0, col0, xcur);
+        if (col0 < p.N && row0 < p.M) epilogue_chunk<EPI>(p, cur, ebuf, row0, col0, xcur, sp);
       }
     }
   }
@@ -615,6 +642,9 @@ int gemm_f16(const GemmCall& g, cudaStream_t stream) {
   args.n_tiles = static_cast<int>((N + bn - 1) / bn);
   args.status = device_status_ptr();
   if (args.status == nullptr) return last_error_code();
+  args.splits = 1;
+  args.kb_per_split = static_cast<int>((K + kGemmBK - 1) / kGemmBK) * g.a_repeat;
+  args.ws = nullptr;
   const long long tiles = static_cast<long long>(args.m_tiles) * args.n_tiles;
   if (pair) {
     const int max_clusters = sms / 2;
@@ -644,6 +674,156 @@ int gemm_f16(const GemmCall& g, cudaStream_t stream) {
   }
   TFB_GEMM_EPI(64, 8)
 #undef TFB_GEMM_EPI
+}
+
+// ---------------------------------------------------------------------------
+// Split-K for few-row problems: the k-blocks of every 128 x 64 tile are cut
+// into `splits` ranges so that tiles x splits CTAs share the work; each unit
+// stores its fp32 partial into the workspace ([splits][M][N]), then a second
+// kernel sums the partials in fixed split order (deterministic), adds the
+// bias and applies the epilogue (fp16 out, GELU, or the fp32 residual add).
+// ---------------------------------------------------------------------------
+template <int EPI>
+__global__ void __launch_bounds__(256) splitk_reduce_kernel(const GemmArgs p) {
+  pdl_wait();
+  pdl_trigger();
+  const int nq = p.N >> 2;  // float4 per row
+  const long long total = static_cast<long long>(p.M) * nq;
+  const long long plane = static_cast<long long>(p.M) * p.N;
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int row = static_cast<int>(i / nq);
+    const int c = static_cast<int>(i - static_cast<long long>(row) * nq) * 4;
+    const float* src = p.ws + static_cast<long long>(row) * p.N + c;
+    float4 a = *reinterpret_cast<const float4*>(src);
+    for (int sp = 1; sp < p.splits; ++sp) {
+      const float4 b = *reinterpret_cast<const float4*>(src + sp * plane);
+      a.x += b.x;
+      a.y += b.y;
+      a.z += b.z;
+      a.w += b.w;
+    }
+    const float4 bq = __ldg(reinterpret_cast<const float4*>(p.bias + c));
+    float v0 = a.x + bq.x, v1 = a.y + bq.y, v2 = a.z + bq.z, v3 = a.w + bq.w;
+    if constexpr (EPI == 2) {
+      const long long off = static_cast<long long>(row) * p.ldx + c;
+      bool valid = true;
+      if (p.mask_mode != 0) valid = p.valid[row] != 0;
+      if (p.mask_mode == 1 && !valid) v0 = v1 = v2 = v3 = 0.f;
+      const float4 x = *reinterpret_cast<const float4*>(p.x_in + off);
+      float4 o = make_float4(x.x + v0, x.y + v1, x.z + v2, x.w + v3);
+      if (p.mask_mode == 2 && !valid) o = make_float4(0.f, 0.f, 0.f, 0.f);
+      *reinterpret_cast<float4*>(p.x_out + off) = o;
+    } else {
+      if constexpr (EPI == 1) {
+        v0 = gelu_erf(v0);
+        v1 = gelu_erf(v1);
+        v2 = gelu_erf(v2);
+        v3 = gelu_erf(v3);
+      }
+      *reinterpret_cast<uint2*>(p.C + static_cast<long long>(row) * p.ldc + c) =
+          make_uint2(pack_half2(v0, v1), pack_half2(v2, v3));
+    }
+  }
+}
+
+// Split count and workspace bytes of a split-K call. splits <= 0: automatic,
+// about one work unit per two SMs and at least two k-blocks (128 of K) per
+// unit (measured on the small model configs: more splits only add partials
+// for the reduce kernel to read).
+static void splitk_plan(long long M, long long N, long long K, int splits_req, int sms, int& splits, int& kps) {
+  const long long tiles = ((M + kGemmBM - 1) / kGemmBM) * ((N + 63) / 64);
+  const int k_blocks = static_cast<int>((K + kGemmBK - 1) / kGemmBK);
+  long long sp = splits_req;
+  if (sp <= 0) {
+    sp = tiles * 2 >= sms ? 1 : sms / (2 * tiles);
+    if (sp > k_blocks / 2) sp = k_blocks / 2;
+  }
+  if (sp > k_blocks) sp = k_blocks;
+  if (sp > kMaxSplits) sp = kMaxSplits;
+  if (sp < 1) sp = 1;
+  kps = static_cast<int>((k_blocks + sp - 1) / sp);
+  splits = (k_blocks + kps - 1) / kps;  // no empty split
+}
+
+long long gemm_splitk_workspace_bytes(long long M, long long N, long long K, int splits_req) {
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  int splits, kps;
+  splitk_plan(M, N, K, splits_req, device_sm_count(), splits, kps);
+  return static_cast<long long>(splits) * M * N * 4;
+}
+
+int gemm_splitk_f16(const GemmCall& g, int splits_req, float* ws, long long ws_bytes, cudaStream_t stream) {
+  const long long M = g.M, N = g.N, K = g.K;
+  if (M <= 0 || N <= 0 || K <= 0) return set_error(TF_ERR_SHAPE, "gemm_splitk: empty shape M=%lld N=%lld K=%lld", M, N, K);
+  if (M > (1ll << 31) - 1 || N > 65535ll * 64 || K > (1 << 24)) return set_error(TF_ERR_SHAPE, "gemm_splitk: shape out of range");
+  if (N % 32 != 0) return set_error(TF_ERR_SHAPE, "gemm_splitk: N=%lld must be a multiple of 32", N);
+  if (g.a_repeat != 1) return set_error(TF_ERR_SHAPE, "gemm_splitk: split weights are not supported");
+  if (g.epilogue < 0 || g.epilogue > 2) return set_error(TF_ERR_SHAPE, "gemm_splitk: epilogue %d", g.epilogue);
+  if (K % 8 != 0 || g.lda % 8 != 0 || g.ldw % 8 != 0)
+    return set_error(TF_ERR_ALIGN, "gemm_splitk: K and leading dimensions must be multiples of 8 elements");
+  if (g.lda < K || g.ldw < K) return set_error(TF_ERR_SHAPE, "gemm_splitk: leading dimension smaller than row");
+  if (!aligned16(g.A) || !aligned16(g.W) || !aligned16(g.bias) || g.A == nullptr || g.W == nullptr ||
+      g.bias == nullptr)
+    return set_error(TF_ERR_ALIGN, "gemm_splitk: A, W and bias must be non-null and 16-byte aligned");
+  if (g.epilogue == 2) {
+    if (g.x_in == nullptr || g.x_out == nullptr || !aligned16(g.x_in) || !aligned16(g.x_out) || g.ldx % 4 != 0 ||
+        g.ldx < N)
+      return set_error(TF_ERR_ALIGN, "gemm_splitk: x_in/x_out must be 16-byte aligned with a pitch >= N, multiple of 4");
+    if (g.mask_mode != 0 && g.valid == nullptr) return set_error(TF_ERR_SHAPE, "gemm_splitk: mask without valid rows");
+  } else if (g.C == nullptr || !aligned16(g.C) || g.ldc % 8 != 0 || g.ldc < N) {
+    return set_error(TF_ERR_ALIGN, "gemm_splitk: C must be 16-byte aligned with a pitch >= N, multiple of 8");
+  }
+  const int sms = device_sm_count();
+  int splits, kps;
+  splitk_plan(M, N, K, splits_req, sms, splits, kps);
+  const long long need = static_cast<long long>(splits) * M * N * 4;
+  if (ws == nullptr || !aligned16(ws) || ws_bytes < need)
+    return set_error(TF_ERR_SHAPE, "gemm_splitk: workspace of %lld bytes (16-byte aligned) needed, %lld given", need,
+                     ws_bytes);
+
+  CUtensorMap ta, tb;
+  int rc = make_tmap_2d_f16(&ta, g.A, K, M, g.lda, kGemmBK, 128);
+  if (rc) return rc;
+  rc = make_tmap_2d_f16(&tb, g.W, K, N, g.ldw, kGemmBK, 64);
+  if (rc) return rc;
+
+  GemmArgs args;
+  args.bias = g.bias;
+  args.C = static_cast<__half*>(g.C);
+  args.ldc = g.ldc;
+  args.x_in = g.x_in;
+  args.x_out = g.x_out;
+  args.ldx = g.ldx;
+  args.valid = g.valid;
+  args.mask_mode = g.epilogue == 2 ? g.mask_mode : 0;
+  args.M = static_cast<int>(M);
+  args.N = static_cast<int>(N);
+  args.K = static_cast<int>(K);
+  args.a_repeat = 1;
+  args.m_tiles = static_cast<int>((M + kGemmBM - 1) / kGemmBM);
+  args.n_tiles = static_cast<int>((N + 63) / 64);
+  args.status = device_status_ptr();
+  if (args.status == nullptr) return last_error_code();
+  args.splits = splits;
+  args.kb_per_split = kps;
+  args.ws = ws;
+  const long long units = static_cast<long long>(args.m_tiles) * args.n_tiles * splits;
+  const int grid = static_cast<int>(units < sms ? units : sms);
+  rc = launch_gemm_cfg<64, 8, 3>(ta, tb, args, grid, stream);
+  if (rc) return rc;
+
+  const long long nq = M * (N / 4);
+  long long blocks = (nq + 255) / 256;
+  if (blocks > 8ll * sms) blocks = 8ll * sms;
+  cudaError_t e;
+  switch (g.epilogue) {
+    case 0: e = launch_k(splitk_reduce_kernel<0>, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, stream, args); break;
+    case 1: e = launch_k(splitk_reduce_kernel<1>, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, stream, args); break;
+    default: e = launch_k(splitk_reduce_kernel<2>, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, stream, args); break;
+  }
+  if (e != cudaSuccess) return set_error(TF_ERR_LAUNCH, "gemm_splitk reduce launch: %s", cudaGetErrorString(e));
+  return TF_OK;
 }
 
 }  // namespace tfb

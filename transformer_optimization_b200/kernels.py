@@ -98,12 +98,30 @@ def split_weight(w: torch.Tensor) -> torch.Tensor:
     return torch.cat([hi, lo], dim=1).contiguous()
 
 
+def splitk_workspace_bytes(m: int, n: int, k: int, splits: int = 0) -> int:
+    """Bytes of fp32 partial sums a split-K call of this shape needs
+    (tf_gemm_splitk_workspace; splits 0 = automatic)."""
+    _abi.load()
+    return int(_abi.call_value("tf_gemm_splitk_workspace", int(m), int(n), int(k), int(splits)))
+
+
+def _splitk_ws(workspace: Optional[torch.Tensor], m: int, n: int, k: int, splits: int, device) -> torch.Tensor:
+    need = splitk_workspace_bytes(m, n, k, splits)
+    if workspace is None:
+        workspace = torch.empty(need, dtype=torch.uint8, device=device)
+    _need_cuda("split-K workspace", workspace)
+    if workspace.numel() * workspace.element_size() < need:
+        raise ValueError(f"split-K workspace of {need} bytes needed")
+    return workspace
+
+
 def linear(a: torch.Tensor, w: torch.Tensor, b: torch.Tensor, *, gelu: bool = False,
            out: Optional[torch.Tensor] = None, tile_n: int = 0, w_split: bool = False,
-           pair: int = 0) -> torch.Tensor:
+           pair: int = 0, splits: Optional[int] = None, workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
     """fp16 GEMM on tcgen05 (tf_gemm): out = fp16([gelu](a @ w.T + b)), a
     [..., K] fp16 with unit inner stride, w [N, K] fp16 (or split_weight's
-    [N, 2K] with w_split), b [N] fp32."""
+    [N, 2K] with w_split), b [N] fp32. splits (0 = automatic) selects the
+    split-K form (tf_gemm_splitk) with `workspace` (allocated if None)."""
     a2, n, k = _gemm_operands("linear", a, w, b, w_split)
     _need_cuda("linear", out)
     m = a2.shape[0]
@@ -112,6 +130,14 @@ def linear(a: torch.Tensor, w: torch.Tensor, b: torch.Tensor, *, gelu: bool = Fa
     o2 = out.view(-1, n) if out.is_contiguous() else out
     if o2.stride(-1) != 1 or o2.dtype != torch.float16:
         raise ValueError("linear: out must be fp16 with a unit inner stride")
+    if splits is not None:
+        if w_split:
+            raise ValueError("linear: split-K does not take split weights")
+        ws = _splitk_ws(workspace, m, n, k, splits, a.device)
+        _abi.call("tf_gemm_splitk", _ptr(a2), a2.stride(0), _ptr(w), w.stride(0), _ptr(b), _ptr(o2), o2.stride(0),
+                  m, n, k, _abi.TF_EPI_BIAS_GELU if gelu else _abi.TF_EPI_BIAS, int(splits), _ptr(ws),
+                  ws.numel() * ws.element_size(), _stream())
+        return out
     epi = (_abi.TF_EPI_BIAS_GELU if gelu else _abi.TF_EPI_BIAS) | (_abi.TF_EPI_W_SPLIT if w_split else 0)
     if tile_n or pair:
         _abi.call("tf_gemm_tiled", _ptr(a2), a2.stride(0), _ptr(w), w.stride(0), _ptr(b), _ptr(o2), o2.stride(0),
@@ -125,10 +151,12 @@ def linear(a: torch.Tensor, w: torch.Tensor, b: torch.Tensor, *, gelu: bool = Fa
 def linear_residual(a: torch.Tensor, w: torch.Tensor, b: torch.Tensor, x_in: torch.Tensor,
                     x_out: Optional[torch.Tensor] = None, valid: Optional[torch.Tensor] = None, *,
                     mask_delta: bool = False, mask_x: bool = False, w_split: bool = False, tile_n: int = 0,
-                    pair: int = 0) -> torch.Tensor:
+                    pair: int = 0, splits: Optional[int] = None,
+                    workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
     """GEMM closing a residual connection in fp32 (tf_gemm_residual):
     x_out = mask_x(x_in + mask_delta(a @ w.T + b)). x_in/x_out fp32 [..., N]
-    contiguous (x_out may be x_in); valid bool/uint8 [rows] for the masks."""
+    contiguous (x_out may be x_in); valid bool/uint8 [rows] for the masks.
+    splits (0 = automatic) selects tf_gemm_residual_splitk."""
     a2, n, k = _gemm_operands("linear_residual", a, w, b, w_split)
     _need_cuda("linear_residual", x_in, x_out, valid)
     if x_in.dtype != torch.float32 or not x_in.is_contiguous() or x_in.shape[-1] != n:
@@ -147,6 +175,14 @@ def linear_residual(a: torch.Tensor, w: torch.Tensor, b: torch.Tensor, x_in: tor
         raise ValueError("linear_residual: masking needs a bool/uint8 mask with one entry per row")
     if valid is not None and not valid.is_contiguous():
         valid = valid.contiguous()
+    if splits is not None:
+        if w_split:
+            raise ValueError("linear_residual: split-K does not take split weights")
+        ws = _splitk_ws(workspace, m, n, k, splits, a.device)
+        _abi.call("tf_gemm_residual_splitk", _ptr(a2), a2.stride(0), _ptr(w), w.stride(0), _ptr(b), _ptr(x_in),
+                  _ptr(x_out), n, _ptr(valid) if mode else None, mode, m, n, k, int(splits), _ptr(ws),
+                  ws.numel() * ws.element_size(), _stream())
+        return x_out
     _abi.call("tf_gemm_residual", _ptr(a2), a2.stride(0), _ptr(w), w.stride(0), _ptr(b), _ptr(x_in), _ptr(x_out), n,
               _ptr(valid) if mode else None, mode, m, n, k, 1 if w_split else 0, tile_n, pair, _stream())
     return x_out

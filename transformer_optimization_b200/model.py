@@ -124,6 +124,16 @@ class _LayerWeights:
             self.b2 = blk.ffn_out.bias.float().contiguous()
 
 
+def _splitk(m: int, n: int, k: int, sms: int) -> Optional[int]:
+    """0 (automatic split count) when a projection of m rows should use the
+    split-K form, else None: fewer than a quarter of the SMs would get a
+    128 x 64 tile and K has at least 8 blocks of 64 to split (measured on
+    the c1/c2 shapes: the 64-row FFN-out drops from 13.5 to 6-7 us; K = 256
+    projections do not gain)."""
+    tiles = -(-m // 128) * -(-n // 64)
+    return 0 if k >= 512 and tiles * 4 < sms else None
+
+
 class _GraphCacheEntry:
     """One captured forward: static input/mask, the graph and its output
     (torch_transformer_benchmark.py:2045-2068)."""
@@ -158,6 +168,7 @@ class UserOptimizedTransformer(BaselineTransformer):
         self._graph_unsupported: set = set()
         self._graph_pool = None
         self._mask_all_true_cache: Dict[Tuple, bool] = {}
+        self._splitk_ws: Optional[torch.Tensor] = None  # fp32 partials of split-K projections
         self.use_cuda_graphs = True
         # FFN-out with split (hi/lo fp16) weights: twice that GEMM's tensor
         # work for a near-fp32 weight. None = automatic (deep stacks only,
@@ -220,18 +231,33 @@ class UserOptimizedTransformer(BaselineTransformer):
         ctx = torch.empty(b, s, d, dtype=torch.float16, device=dev)
         hidden = torch.empty(b, s, cfg.ffn_dim, dtype=torch.float16, device=dev)
 
+        # split-K (fp32 partials in a workspace) for the projections of
+        # few-row inputs, where 128-row tiles would leave most SMs idle
+        m, f = b * s, cfg.ffn_dim
+        sms = torch.cuda.get_device_properties(dev).multi_processor_count
+        sk_qkv, sk_o, sk_1 = _splitk(m, 3 * d, d, sms), _splitk(m, d, d, sms), _splitk(m, f, d, sms)
+        sk_2 = None if wts[0].split_w2 else _splitk(m, d, f, sms)
+        ws = None
+        if any(v is not None for v in (sk_qkv, sk_o, sk_1, sk_2)):
+            need = max(kernels.splitk_workspace_bytes(m, n, k)
+                       for n, k, v in ((3 * d, d, sk_qkv), (d, d, sk_o), (f, d, sk_1), (d, f, sk_2)) if v is not None)
+            ws = self._splitk_ws
+            if ws is None or ws.device != dev or ws.numel() < need:
+                ws = self._splitk_ws = torch.empty(need, dtype=torch.uint8, device=dev)
+
         cur = x  # residual stream; the caller's x is read, never written
         for li, blk in enumerate(self.layers):
             w = wts[li]
             kernels.ln_residual(cur, None, blk.norm1.weight, blk.norm1.bias, blk.norm1.eps, normed=normed)
-            kernels.linear(normed, w.wqkv, w.bqkv, out=qkv)
+            kernels.linear(normed, w.wqkv, w.bqkv, out=qkv, splits=sk_qkv, workspace=ws)
             kernels.flash_attention(qkv[..., :d], qkv[..., d:2 * d], qkv[..., 2 * d:], h, scale,
                                     causal=cfg.causal, key_valid=kvalid, out=ctx)
-            cur = kernels.linear_residual(ctx, w.wo, w.bo, cur, x_res, vflat, mask_delta=mask_active)
+            cur = kernels.linear_residual(ctx, w.wo, w.bo, cur, x_res, vflat, mask_delta=mask_active,
+                                          splits=sk_o, workspace=ws)
             kernels.ln_residual(cur, None, blk.norm2.weight, blk.norm2.bias, blk.norm2.eps, normed=normed)
-            kernels.linear(normed, w.w1, w.b1, gelu=True, out=hidden)
+            kernels.linear(normed, w.w1, w.b1, gelu=True, out=hidden, splits=sk_1, workspace=ws)
             kernels.linear_residual(hidden, w.w2, w.b2, cur, x_res, vflat, mask_x=mask_active,
-                                    w_split=w.split_w2)
+                                    w_split=w.split_w2, splits=sk_2, workspace=ws)
         fn = self.final_norm
         _, out = kernels.ln_residual(cur, None, fn.weight, fn.bias, fn.eps, vflat, mask_out=mask_active,
                                      out_dtype=torch.float32)
