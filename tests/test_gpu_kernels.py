@@ -63,6 +63,32 @@ def test_ln_residual(K, m, d, flags):
         assert torch.allclose(y.float().cpu(), yr.half().float(), atol=2e-3, rtol=1e-3)
 
 
+@pytest.mark.parametrize("d", [256, 1024, 2048])
+@pytest.mark.parametrize("flags", ["plain", "delta", "mask_x"])
+def test_ln_residual_stream_ring(K, d, flags):
+    """Enough rows that every CTA of the streaming LayerNorm cycles its
+    shared-memory ring many times (about 12 groups of 8 rows per SM), for the
+    two- and three-team configurations (D 2048: two teams and two stages with
+    delta, three and three without; D 1024 with delta: two teams, four
+    stages; narrower: three teams, six stages)."""
+    m = 148 * 8 * 12 + 5
+    g = torch.Generator().manual_seed(d + len(flags))
+    x = torch.randn(m, d, generator=g) * 2 + 0.5
+    delta = (torch.randn(m, d, generator=g) * 0.5).half()
+    w = torch.randn(d, generator=g) * 0.1 + 1
+    b = torch.randn(d, generator=g) * 0.1
+    valid = torch.rand(m, generator=g) > 0.3
+    use_delta = flags != "plain"
+    mx = flags == "mask_x"
+    xr, yr = om.ln_site(x, delta if use_delta else None, w, b, 1e-5, valid, False, mx, False)
+    dv = _dev()
+    x_new, y = K.ln_residual(x.to(dv), delta.to(dv) if use_delta else None, w.to(dv), b.to(dv), 1e-5, valid.to(dv),
+                             mask_x=mx, write_x=use_delta)
+    if use_delta:
+        assert torch.equal(x_new.cpu(), xr)
+    assert torch.allclose(y.float().cpu(), yr.half().float(), atol=2e-3, rtol=1e-3)
+
+
 def test_ln_residual_in_place(K):
     g = torch.Generator().manual_seed(5)
     x = torch.randn(300, 1024, generator=g)

@@ -15,8 +15,8 @@
 //    8 rows through a ring of shared-memory stages filled by the bulk-copy
 //    engine (cp.async.bulk, one copy for the 8 x rows and one for the 8 delta
 //    rows of a group), so ~100-200 KB per SM are in flight independent of
-//    registers; two teams of 8 consumer warps take alternate groups, one row
-//    per warp, and store the results straight to HBM.
+//    registers; two or three teams of 8 consumer warps take successive
+//    groups, one row per warp, and store the results straight to HBM.
 //  * ln_residual_kernel (any D up to 4096): one warp per row with the row in
 //    registers, grid-stride over rows.
 #include "common.cuh"
@@ -134,9 +134,9 @@ __global__ void __launch_bounds__(256) ln_residual_kernel(const float* __restric
 // Streaming variant: bulk-copy ring of 8-row groups
 // ---------------------------------------------------------------------------
 constexpr int kLnsRows = 8;        // rows per group (one consumer warp each)
-constexpr int kLnsTeams = 2;       // consumer teams working on alternate groups
-constexpr int kLnsThreads = 32 * (kLnsRows * kLnsTeams + 1);  // + 1 producer warp
 constexpr int kLnsMaxStages = 8;
+// TEAMS consumer teams of 8 warps work on successive groups, + 1 producer warp
+__host__ __device__ constexpr int lns_threads(int teams) { return 32 * (kLnsRows * teams + 1); }
 constexpr int kLnsSmemBudget = 196608;
 
 struct LnsParams {
@@ -153,8 +153,13 @@ struct LnsParams {
   int* status;
 };
 
-template <int NV>  // float4 per lane (row width up to 128*NV)
-__global__ void __launch_bounds__(kLnsThreads, 1) ln_stream_kernel(const LnsParams p) {
+// Stage ownership: group number `it` (this CTA's it-th group) goes to stage
+// it % stages and to team it % TEAMS. The host makes stages a multiple of
+// TEAMS, so every stage is only ever used by one team, whose waits on it come
+// in phase order: an mbarrier waiter that could fall two phases behind would
+// see the parity of an older phase and read a stage that is being refilled.
+template <int NV, int TEAMS>  // NV: float4 per lane (row width up to 128*NV)
+__global__ void __launch_bounds__(lns_threads(TEAMS), 1) ln_stream_kernel(const LnsParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
   const int D = p.D;
@@ -165,6 +170,10 @@ __global__ void __launch_bounds__(kLnsThreads, 1) ln_stream_kernel(const LnsPara
   uint64_t* empty = full + kLnsMaxStages;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long long groups = (p.M + kLnsRows - 1) / kLnsRows;
+  if (p.stages % TEAMS != 0 || p.stages > kLnsMaxStages) {  // host invariant; refuse rather than race
+    if (threadIdx.x == 0) record_error(p.status, kDevTimeoutProducer);
+    return;
+  }
   if (threadIdx.x == 0) {
     for (int i = 0; i < p.stages; ++i) {
       mbar_init(&full[i], 1);
@@ -176,7 +185,7 @@ __global__ void __launch_bounds__(kLnsThreads, 1) ln_stream_kernel(const LnsPara
   pdl_wait();
   pdl_trigger();
 
-  if (warp == kLnsRows * kLnsTeams) {
+  if (warp == kLnsRows * TEAMS) {
     // ---------------- producer ----------------
     if (lane == 0) {
       int it = 0;
@@ -197,13 +206,13 @@ __global__ void __launch_bounds__(kLnsThreads, 1) ln_stream_kernel(const LnsPara
   }
 
   // ---------------- consumers ----------------
-  // team k = warp / 8 takes this CTA's groups k, k+2, k+4, ...; warp w of
-  // the team takes row w % 8 of each
+  // team k = warp / 8 takes this CTA's groups k, k+TEAMS, ...; warp w of the
+  // team takes row w % 8 of each
   const int nv = D >> 2;  // float4 per row
   const int team = warp / kLnsRows, wr = warp % kLnsRows;
   int it = team;
   for (long long g = blockIdx.x + static_cast<long long>(team) * gridDim.x; g < groups;
-       g += static_cast<long long>(kLnsTeams) * gridDim.x, it += kLnsTeams) {
+       g += static_cast<long long>(TEAMS) * gridDim.x, it += TEAMS) {
     const int s = it % p.stages;
     const long long row = g * kLnsRows + wr;
     const bool have = row < p.M;
@@ -312,8 +321,15 @@ int ln_residual(const float* x, const void* delta, const float* w, const float* 
     lp.status = device_status_ptr();
     if (lp.status == nullptr) return last_error_code();
     const int stage_bytes = kLnsRows * D * (delta != nullptr ? 6 : 4);
-    int stages = kLnsSmemBudget / stage_bytes;
-    stages = stages > kLnsMaxStages ? kLnsMaxStages : (stages < 2 ? 2 : stages);
+    // teams and stages (a multiple of the team count, see the kernel's
+    // stage-ownership note), best measured at the c3/c4 shapes: three teams
+    // with six stages (D <= 1024 without delta), two with four (D = 1024 with
+    // delta), three with three (D = 2048), two with two (D = 2048 with delta)
+    int fit = kLnsSmemBudget / stage_bytes;
+    if (fit > kLnsMaxStages) fit = kLnsMaxStages;
+    const int teams = (fit >= 6 || fit == 3) ? 3 : 2;
+    const int stages = (fit / teams) * teams;
+    if (stages < teams) return set_error(TF_ERR_SHAPE, "ln_residual: D=%d too wide for the streaming kernel", D);
     lp.stages = stages;
     const int smem = stages * stage_bytes + 2 * kLnsMaxStages * 8 + 128;
     const long long groups = (M + kLnsRows - 1) / kLnsRows;
@@ -321,24 +337,29 @@ int ln_residual(const float* x, const void* delta, const float* w, const float* 
     const int nv = (D / 4 + 31) / 32;
     int dev = 0;
     cudaGetDevice(&dev);
-#define TFB_LNS_CASE(N)                                                                             \
+#define TFB_LNS_CASE(N, T)                                                                          \
   {                                                                                                 \
     static bool attr_done[64] = {};                                                                 \
     if (!attr_done[dev & 63]) {                                                                     \
-      cudaError_t ea = cudaFuncSetAttribute(ln_stream_kernel<N>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+      cudaError_t ea = cudaFuncSetAttribute(ln_stream_kernel<N, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
                                             kLnsSmemBudget + 2 * kLnsMaxStages * 8 + 128);          \
       if (ea != cudaSuccess)                                                                        \
         return set_error(TF_ERR_LAUNCH, "cudaFuncSetAttribute(ln): %s", cudaGetErrorString(ea));    \
       attr_done[dev & 63] = true;                                                                   \
     }                                                                                               \
-    launch_k(ln_stream_kernel<N>, dim3(static_cast<unsigned>(grid)), dim3(kLnsThreads), smem, stream, lp); \
+    launch_k(ln_stream_kernel<N, T>, dim3(static_cast<unsigned>(grid)), dim3(lns_threads(T)), smem, stream, lp); \
   }                                                                                                 \
   break;
-    switch (nv <= 2 ? 2 : nv <= 4 ? 4 : nv <= 8 ? 8 : 16) {
-      case 2: TFB_LNS_CASE(2)
-      case 4: TFB_LNS_CASE(4)
-      case 8: TFB_LNS_CASE(8)
-      default: TFB_LNS_CASE(16)
+    const int nvc = nv <= 2 ? 2 : nv <= 4 ? 4 : nv <= 8 ? 8 : 16;
+    switch (nvc * 10 + teams) {
+      case 22: TFB_LNS_CASE(2, 2)
+      case 23: TFB_LNS_CASE(2, 3)
+      case 42: TFB_LNS_CASE(4, 2)
+      case 43: TFB_LNS_CASE(4, 3)
+      case 82: TFB_LNS_CASE(8, 2)
+      case 83: TFB_LNS_CASE(8, 3)
+      case 162: TFB_LNS_CASE(16, 2)
+      default: TFB_LNS_CASE(16, 3)
     }
 #undef TFB_LNS_CASE
     cudaError_t e = cudaGetLastError();

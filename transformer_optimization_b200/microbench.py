@@ -57,6 +57,7 @@ def main(argv=None):
     ap.add_argument("dims", type=int, nargs="+")
     ap.add_argument("--gelu", action="store_true")
     ap.add_argument("--causal", action="store_true")
+    ap.add_argument("--pure", action="store_true", help="ln: LayerNorm only (no residual delta, no x write)")
     ap.add_argument("--exp-f16x2", action="store_true", help="flash: packed fp16 exp2 path")
     ap.add_argument("--fma-exp", type=int, default=0, help="flash: pairs per row exponentiated on the FMA pipes")
     ap.add_argument("--tile-n", type=int, default=0)
@@ -107,8 +108,12 @@ def main(argv=None):
         b = torch.zeros(d, device=dev)
         xo = torch.empty_like(x)
         nrm = torch.empty(m, d, device=dev, dtype=torch.float16)
-        ms = T(lambda: K.ln_residual(x, delta, w, b, 1e-5, write_x=True, x_out=xo, normed=nrm))
-        print(f"ln M={m} D={d}: {ms:.4f} ms  {m * d * 12 / (ms / 1e3) / 1e9:.1f} GB/s")
+        if a.pure:  # the model's LayerNorm sites: read x, write fp16 normed
+            ms = T(lambda: K.ln_residual(x, None, w, b, 1e-5, normed=nrm))
+            print(f"ln (pure) M={m} D={d}: {ms:.4f} ms  {m * d * 6 / (ms / 1e3) / 1e9:.1f} GB/s")
+        else:
+            ms = T(lambda: K.ln_residual(x, delta, w, b, 1e-5, write_x=True, x_out=xo, normed=nrm))
+            print(f"ln M={m} D={d}: {ms:.4f} ms  {m * d * 12 / (ms / 1e3) / 1e9:.1f} GB/s")
 
 
 if __name__ == "__main__":
