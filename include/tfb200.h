@@ -140,6 +140,24 @@ int tf_gemm_residual_splitk(const void* A, int64_t lda, const void* W, int64_t l
                             int64_t M, int64_t N, int64_t K, int splits, void* workspace, int64_t workspace_bytes,
                             void* stream);
 
+/* tf_gemm_splitk without a workspace argument: the fp32 partial sums go to a
+ * fixed 4 MiB device array inside this library, so the call allocates
+ * nothing and needs no caller-provided memory. For callers that cannot
+ * allocate device memory at the point of the call: code that must not call
+ * an allocator there (cudaMalloc synchronises the device and is not
+ * permitted while a stream is being captured), and foreign-language hosts
+ * that have no device allocator to hand a workspace through the C
+ * interface. Limit: splits * M * N * 4 bytes (tf_gemm_splitk_workspace)
+ * must not exceed 4 MiB; larger calls return TF_ERR_SHAPE. The array is one
+ * per device and shared by all calls: calls that overlap in time (on
+ * different streams or from different host threads) race on it and must be
+ * serialised by the caller. The first call on each device looks up the
+ * array's address (cudaGetSymbolAddress, once, with that device current);
+ * make that first call before any stream capture. No reference counterpart:
+ * the reference has no FFI and allocates its temporaries through PyTorch. */
+int tf_gemm_splitk_static(const void* A, int64_t lda, const void* W, int64_t ldw, const float* bias, void* C,
+                          int64_t ldc, int64_t M, int64_t N, int64_t K, int epilogue, int splits, void* stream);
+
 /* Flash attention forward (online softmax, no score matrix in HBM):
  *   out[b, i, h*hd:(h+1)*hd] = sum_j softmax_j(scale * q_i . k_j) v_j
  * q: fp16, token i of batch b, head h at q + b*bs_q + i*ld_q + h*hd;

@@ -166,7 +166,7 @@ static inline int begin_call() {
 
 extern "C" {
 
-int tf_abi_version(void) { return 6; }
+int tf_abi_version(void) { return 7; }
 
 const char* tf_last_error(void) { return tfb::g_msg; }
 
@@ -294,6 +294,28 @@ int tf_gemm_splitk(const void* A, int64_t lda, const void* W, int64_t ldw, const
   g.epilogue = epilogue;
   g.a_repeat = 1;
   return tfb::gemm_splitk_f16(g, splits, static_cast<float*>(workspace), workspace_bytes, as_stream(stream));
+}
+
+int tf_gemm_splitk_static(const void* A, int64_t lda, const void* W, int64_t ldw, const float* bias, void* C,
+                          int64_t ldc, int64_t M, int64_t N, int64_t K, int epilogue, int splits, void* stream) {
+  int rc = begin_call();
+  if (rc) return rc;
+  if (epilogue != TF_EPI_BIAS && epilogue != TF_EPI_BIAS_GELU)
+    return set_error(TF_ERR_SHAPE, "tf_gemm_splitk_static: epilogue=%d (TF_EPI_BIAS or TF_EPI_BIAS_GELU)", epilogue);
+  tfb::GemmCall g = {};
+  g.A = A;
+  g.lda = lda;
+  g.W = W;
+  g.ldw = ldw;
+  g.bias = bias;
+  g.C = C;
+  g.ldc = ldc;
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.epilogue = epilogue;
+  g.a_repeat = 1;
+  return tfb::gemm_splitk_static_f16(g, splits, as_stream(stream));
 }
 
 int tf_gemm_residual_splitk(const void* A, int64_t lda, const void* W, int64_t ldw, const float* bias,

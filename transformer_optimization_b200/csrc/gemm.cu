@@ -25,6 +25,8 @@
 //   warps 2..5  epilogue: tcgen05.ld of the accumulator, bias/GELU, stores
 // The accumulator is double-buffered in TMEM (2 x BN fp32 columns) so the
 // epilogue of tile i overlaps the main loop of tile i+1.
+#include <mutex>
+
 #include "common.cuh"
 #include "launch.h"
 
@@ -824,6 +826,44 @@ int gemm_splitk_f16(const GemmCall& g, int splits_req, float* ws, long long ws_b
   }
   if (e != cudaSuccess) return set_error(TF_ERR_LAUNCH, "gemm_splitk reduce launch: %s", cudaGetErrorString(e));
   return TF_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Split-K with library-owned scratch: the fp32 partials go to a fixed device
+// array of this library instead of a caller workspace, for callers that
+// cannot allocate device memory (see tf_gemm_splitk_static).
+// ---------------------------------------------------------------------------
+constexpr long long kStaticScratchBytes = 4ll << 20;  // 4 MiB of fp32 partial sums
+static __device__ __align__(256) float g_splitk_scratch[kStaticScratchBytes / 4];
+
+int gemm_splitk_static_f16(const GemmCall& g, int splits, cudaStream_t stream) {
+  static std::mutex mu;
+  static float* ptrs[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(TF_ERR_DEVICE, "cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= 64) return set_error(TF_ERR_DEVICE, "device ordinal %d out of range", dev);
+  float* scratch;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (ptrs[dev] == nullptr) {
+      // once per device, with that device current: the address of this
+      // device's copy of the array (no allocation; the array is part of the
+      // library's device image)
+      void* a = nullptr;
+      e = cudaGetSymbolAddress(&a, g_splitk_scratch);
+      if (e != cudaSuccess) return set_error(TF_ERR_DEVICE, "cudaGetSymbolAddress(scratch): %s", cudaGetErrorString(e));
+      ptrs[dev] = static_cast<float*>(a);
+    }
+    scratch = ptrs[dev];
+  }
+  const long long need = gemm_splitk_workspace_bytes(g.M, g.N, g.K, splits);
+  if (need > kStaticScratchBytes)
+    return set_error(TF_ERR_SHAPE, "gemm_splitk_static: %lld bytes of partial sums exceed the %lld-byte scratch", need,
+                     kStaticScratchBytes);
+  // every partial element a call reads is written by the same call first, so
+  // the scratch needs no clearing between calls
+  return gemm_splitk_f16(g, splits, scratch, kStaticScratchBytes, stream);
 }
 
 }  // namespace tfb

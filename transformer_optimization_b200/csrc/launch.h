@@ -84,6 +84,8 @@ int gemm_f16(const GemmCall& g, cudaStream_t stream);
 // split-K GEMM (epilogues 0, 1, 2) with an fp32 partial-sum workspace
 int gemm_splitk_f16(const GemmCall& g, int splits, float* ws, long long ws_bytes, cudaStream_t stream);
 long long gemm_splitk_workspace_bytes(long long M, long long N, long long K, int splits);
+// the same with the library's fixed 4 MiB device scratch (no allocation)
+int gemm_splitk_static_f16(const GemmCall& g, int splits, cudaStream_t stream);
 
 int ln_residual(const float* x, const void* delta, const float* w, const float* b, float eps,
                 const uint8_t* valid, long long M, int D, int flags, float* x_out, void* normed,
