@@ -166,7 +166,10 @@ __global__ void __launch_bounds__(lns_threads(TEAMS), 1) ln_stream_kernel(const 
   const bool has_delta = p.delta != nullptr;
   const uint32_t x_bytes = static_cast<uint32_t>(kLnsRows) * D * 4;
   const uint32_t stage_bytes = x_bytes + (has_delta ? static_cast<uint32_t>(kLnsRows) * D * 2 : 0u);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.stages * stage_bytes);
+  // LayerNorm weight and bias staged once per CTA (read by every row)
+  float* w_s = reinterpret_cast<float*>(smem + p.stages * stage_bytes);
+  float* b_s = w_s + D;
+  uint64_t* full = reinterpret_cast<uint64_t*>(b_s + D);
   uint64_t* empty = full + kLnsMaxStages;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long long groups = (p.M + kLnsRows - 1) / kLnsRows;
@@ -181,9 +184,13 @@ __global__ void __launch_bounds__(lns_threads(TEAMS), 1) ln_stream_kernel(const 
     }
     fence_mbar_init();
   }
-  __syncthreads();
   pdl_wait();
   pdl_trigger();
+  for (int i = threadIdx.x; i < (D >> 2); i += blockDim.x) {
+    reinterpret_cast<float4*>(w_s)[i] = __ldg(reinterpret_cast<const float4*>(p.w) + i);
+    reinterpret_cast<float4*>(b_s)[i] = __ldg(reinterpret_cast<const float4*>(p.b) + i);
+  }
+  __syncthreads();
 
   if (warp == kLnsRows * TEAMS) {
     // ---------------- producer ----------------
@@ -268,8 +275,8 @@ __global__ void __launch_bounds__(lns_threads(TEAMS), 1) ln_stream_kernel(const 
         if (c < nv) {
           if (p.flags & TF_LN_WRITE_X)
             __stcs(reinterpret_cast<float4*>(p.x_out + row * D) + c, make_float4(v[i][0], v[i][1], v[i][2], v[i][3]));
-          const float4 wv = __ldg(reinterpret_cast<const float4*>(p.w) + c);
-          const float4 bv = __ldg(reinterpret_cast<const float4*>(p.b) + c);
+          const float4 wv = reinterpret_cast<const float4*>(w_s)[c];
+          const float4 bv = reinterpret_cast<const float4*>(b_s)[c];
           float y0 = (v[i][0] - mean) * rstd * wv.x + bv.x;
           float y1 = (v[i][1] - mean) * rstd * wv.y + bv.y;
           float y2 = (v[i][2] - mean) * rstd * wv.z + bv.z;
@@ -331,7 +338,7 @@ int ln_residual(const float* x, const void* delta, const float* w, const float* 
     const int stages = (fit / teams) * teams;
     if (stages < teams) return set_error(TF_ERR_SHAPE, "ln_residual: D=%d too wide for the streaming kernel", D);
     lp.stages = stages;
-    const int smem = stages * stage_bytes + 2 * kLnsMaxStages * 8 + 128;
+    const int smem = stages * stage_bytes + 8 * D + 2 * kLnsMaxStages * 8 + 128;
     const long long groups = (M + kLnsRows - 1) / kLnsRows;
     const long long grid = groups < device_sm_count() ? groups : device_sm_count();
     const int nv = (D / 4 + 31) / 32;
@@ -342,7 +349,7 @@ int ln_residual(const float* x, const void* delta, const float* w, const float* 
     static bool attr_done[64] = {};                                                                 \
     if (!attr_done[dev & 63]) {                                                                     \
       cudaError_t ea = cudaFuncSetAttribute(ln_stream_kernel<N, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
-                                            kLnsSmemBudget + 2 * kLnsMaxStages * 8 + 128);          \
+                                            kLnsSmemBudget + 8 * 2048 + 2 * kLnsMaxStages * 8 + 128); \
       if (ea != cudaSuccess)                                                                        \
         return set_error(TF_ERR_LAUNCH, "cudaFuncSetAttribute(ln): %s", cudaGetErrorString(ea));    \
       attr_done[dev & 63] = true;                                                                   \
