@@ -76,6 +76,18 @@ struct GemmSmem {
 // ways) so that the global accesses run along rows: lane L handles columns
 // 4*(L%8)..+3 of rows it*4 + L/8, i.e. each store instruction covers 4 rows
 // x 64 B (fp16) or 4 rows x 128 B (fp32) instead of 32 scattered rows.
+// L2 prefetch of this warp's residual rows for a whole tile (EPI 2): lane L
+// touches row row0 + L, `width` columns from col0, one 128-byte line at a
+// time. Issued before the warp waits for the tile's accumulator, so the HBM
+// reads overlap the tile's main loop and the register loads below hit L2.
+__device__ __forceinline__ void prefetch_residual_l2(const GemmArgs& p, int row0, int col0, int width) {
+  const int row = row0 + (threadIdx.x & 31);
+  if (row >= p.M) return;
+  const float* base = p.x_in + static_cast<long long>(row) * p.ldx;
+  for (int c = col0; c < col0 + width && c < p.N; c += 32)
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(base + c));
+}
+
 // Residual rows of one chunk for this lane (EPI 2): rows row0 + it*4 + L/8,
 // columns col0 + 4*(L%8), it = 0..7. Issued ahead of use so the HBM latency
 // overlaps the previous chunk.
@@ -273,9 +285,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int n0 = (t % p.n_tiles) * BN;
       const int a = tc & 1;
       const uint32_t aph = (tc >> 1) & 1;
+      const int row0 = m0 + quarter * 32;
+      if constexpr (EPI == 2) prefetch_residual_l2(p, row0, n0, BN);
       if (!mbar_wait(&tfull[a], aph, p.status, kDevTimeoutEpilogue)) break;
       tc_fence_after();
-      const int row0 = m0 + quarter * 32;
       const uint32_t t_addr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + a * BN;
       float4 xa[8], xb[8];
       if constexpr (EPI == 2) {
@@ -467,9 +480,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemm2Threads, 1)
       const int n0 = (t % p.n_tiles) * BN + half * (BN / 2);
       const int a = tc & 1;
       const uint32_t aph = (tc >> 1) & 1;
+      const int row0 = m0 + quarter * 32;
+      if constexpr (EPI == 2) prefetch_residual_l2(p, row0, n0, BN / 2);
       if (!mbar_wait(&tfull[a], aph, p.status, kDevTimeoutEpilogue)) break;
       tc_fence_after();
-      const int row0 = m0 + quarter * 32;
       const uint32_t t_addr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + a * BN + half * (BN / 2);
       constexpr int NCH = BN / 64;  // 32-column chunks per half
       float4 xa[8], xb[8];
