@@ -155,6 +155,44 @@ def time_steps(fn, steps, flush_buf):
     return [s.elapsed_time(e) for s, e in zip(starts, ends)]
 
 
+def e2e_pipelined(model, x_host, y_host, steps, device):
+    """`steps` forward passes through the public module, each with its own
+    host-to-device copy of the pinned input and device-to-host copy of the
+    output, as a serving loop runs them: the copies go on two copy streams
+    (double-buffered device input), so step i+1's upload and step i-1's
+    download overlap step i's forward. One CUDA-event pair brackets the whole
+    sequence, first upload to last download. Returns the total in ms."""
+    comp = torch.cuda.current_stream(device)
+    up, down = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    xd = [torch.empty(x_host.shape, dtype=x_host.dtype, device=device) for _ in range(2)]
+    ev = lambda: torch.cuda.Event()  # noqa: E731
+    fwd_done = [None] * steps
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(comp)
+    up.wait_event(start)
+    down.wait_event(start)
+    for i in range(steps):
+        b = i % 2
+        with torch.cuda.stream(up):
+            if i >= 2:
+                up.wait_event(fwd_done[i - 2])  # the forward that read this buffer is done
+            xd[b].copy_(x_host, non_blocking=True)
+            uploaded = ev()
+            uploaded.record(up)
+        comp.wait_event(uploaded)
+        y = model(xd[b])
+        fwd_done[i] = ev()
+        fwd_done[i].record(comp)
+        with torch.cuda.stream(down):
+            down.wait_event(fwd_done[i])
+            y_host.copy_(y, non_blocking=True)
+            y.record_stream(down)
+    comp.wait_stream(down)
+    end.record(comp)
+    torch.cuda.synchronize()
+    return start.elapsed_time(end)
+
+
 def kernel_profile(model, x):
     """One instrumented eager forward: CUDA events around every launch of the
     GEMM, attention and LayerNorm kernels (on the launching stream).
@@ -319,19 +357,12 @@ def run_ours(args, cfg, rank, world, local_rank):
     # ---- end to end through the public module: pinned host in, host out ----
     x_host = torch.randn(cfg.batch_size, cfg.seq_len, cfg.d_model).pin_memory()
     y_host = torch.empty_like(x_host).pin_memory()
-
-    def e2e_step():
-        xd = x_host.to(device, non_blocking=True)
-        y = model(xd)
-        y_host.copy_(y, non_blocking=True)
-
     with torch.inference_mode():
-        e2e_step()
+        e2e_pipelined(model, x_host, y_host, 2, device)  # warm-up (allocations, streams)
         torch.cuda.synchronize()
         if dist is not None:
             dist.barrier()
-        e_ts = time_steps(e2e_step, args.steps, flush_buf)
-    e_total = sum(e_ts)
+        e_total = e2e_pipelined(model, x_host, y_host, args.steps, device)
     if dist is not None:
         t = torch.tensor([e_total], device=device, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -363,7 +394,9 @@ def run_ours(args, cfg, rank, world, local_rank):
         "mfu": flops / (ms_per_step / 1e3) / (tensor_peak * 1e12),
         "latency_ms": ms_per_step, "latency_ms_median": statistics.median(ts),
         "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": x_host.numel() * 4,
-                "d2h_bytes_per_step": y_host.numel() * 4, "ms_per_step": e_total / args.steps},
+                "d2h_bytes_per_step": y_host.numel() * 4, "ms_per_step": e_total / args.steps,
+                "copies": "pinned H2D and D2H every step on two copy streams, overlapping the neighbouring "
+                          "steps' forwards; one event pair from the first upload to the last download"},
         "gpu_launches": launches_per_step * args.steps,
         "roofline": {"bound": "tensor", "kernel": "gemm_f16_tcgen05", "achieved": gemm_tflops,
                      "peak": sustained, "unit": "TFLOP/s", "frac": gemm_tflops / sustained,
