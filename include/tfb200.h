@@ -148,10 +148,12 @@ int tf_gemm_residual_splitk(const void* A, int64_t lda, const void* W, int64_t l
  * permitted while a stream is being captured), and foreign-language hosts
  * that have no device allocator to hand a workspace through the C
  * interface. Limit: splits * M * N * 4 bytes (tf_gemm_splitk_workspace)
- * must not exceed 4 MiB; larger calls return TF_ERR_SHAPE. The array is one
- * per device and shared by all calls: calls that overlap in time (on
- * different streams or from different host threads) race on it and must be
- * serialised by the caller. The first call on each device looks up the
+ * must not exceed 4 MiB; larger calls return TF_ERR_SHAPE. Every GPU that
+ * loads the library holds its copy of the array until the process exits. The
+ * array is shared by all calls on a device and keeps the last call's
+ * contents (a call writes every partial it reads, so nothing needs
+ * clearing); calls that overlap on the GPU (on different streams or from
+ * different host threads) race on it and must be serialised by the caller. The first call on each device looks up the
  * array's address (cudaGetSymbolAddress, once, with that device current);
  * make that first call before any stream capture. No reference counterpart:
  * the reference has no FFI and allocates its temporaries through PyTorch. */
