@@ -35,7 +35,7 @@ namespace tfb {
 constexpr int kGemmBM = 128;
 constexpr int kGemmBK = 64;  // one 128-byte swizzle row of fp16
 constexpr int kGemmThreads = 192;
-constexpr int kEpiTileFloats = 32 * 33;  // one warp's epilogue staging tile
+constexpr int kEpiTileFloats = 32 * 32;  // one warp's epilogue staging tile (32 x 32 fp32)
 constexpr int kMaxSplits = 32;           // split-K: most k ranges per tile
 
 struct GemmArgs {
@@ -70,12 +70,6 @@ struct GemmSmem {
   static constexpr int kAlloc = kBytes + 1024;  // slack for 1024-byte alignment
 };
 
-// Epilogue of one 32-row x 32-column accumulator chunk, cooperatively by the
-// warp that read it from TMEM (lane i holds row row0+i). The chunk is staged
-// through a padded shared-memory tile (32 x 33 floats, conflict-free both
-// ways) so that the global accesses run along rows: lane L handles columns
-// 4*(L%8)..+3 of rows it*4 + L/8, i.e. each store instruction covers 4 rows
-// x 64 B (fp16) or 4 rows x 128 B (fp32) instead of 32 scattered rows.
 // L2 prefetch of this warp's residual rows for a whole tile (EPI 2): lane L
 // touches row row0 + L, `width` columns from col0, one 128-byte line at a
 // time. Issued before the warp waits for the tile's accumulator, so the HBM
@@ -102,12 +96,26 @@ __device__ __forceinline__ void load_residual(const GemmArgs& p, float4 (&xv)[8]
   }
 }
 
+// Epilogue of one 32-row x 32-column accumulator chunk, cooperatively by the
+// warp that read it from TMEM (lane i holds row row0+i). The chunk is staged
+// through a 32 x 32 float shared-memory tile (16-byte chunks XOR-swizzled by
+// row, conflict-free both ways) so that the global accesses run along rows:
+// lane L handles columns 4*(L%8)..+3 of rows it*4 + L/8, i.e. each store
+// instruction covers 4 rows x 64 B (fp16) or 4 rows x 128 B (fp32) instead of
+// 32 scattered rows.
 template <int EPI>
 __device__ __forceinline__ void epilogue_chunk(const GemmArgs& p, const uint32_t (&r)[32], float* buf, int row0,
                                                int col0, const float4 (&xv)[8], int split = 0) {
   const int lane = threadIdx.x & 31;
+  // 16-byte chunk c of row r sits at chunk c ^ (r % 8) of the row's 128 bytes:
+  // both the row-wise writes (lanes = rows) and the column-wise reads below
+  // (8 lanes = one row's 8 chunks) touch 8 different chunks per quarter-warp,
+  // so the vector accesses are free of bank conflicts without padding
+  float4* tile = reinterpret_cast<float4*>(buf);
 #pragma unroll
-  for (int i = 0; i < 32; ++i) buf[lane * 33 + i] = __uint_as_float(r[i]);
+  for (int c = 0; c < 8; ++c)
+    tile[lane * 8 + (c ^ (lane & 7))] = make_float4(__uint_as_float(r[4 * c]), __uint_as_float(r[4 * c + 1]),
+                                                    __uint_as_float(r[4 * c + 2]), __uint_as_float(r[4 * c + 3]));
   __syncwarp();
   const int c4 = (lane & 7) * 4;
   const float4 bq = __ldg(reinterpret_cast<const float4*>(p.bias + col0 + c4));
@@ -115,7 +123,8 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& p, const uint32_t
   for (int it = 0; it < 8; ++it) {
     const int rl = it * 4 + (lane >> 3);
     const int row = row0 + rl;
-    const float* src = buf + rl * 33 + c4;
+    const float4 a = tile[rl * 8 + ((lane & 7) ^ (rl & 7))];
+    const float src[4] = {a.x, a.y, a.z, a.w};
     if constexpr (EPI == 3) {
       // split-K partial: the raw fp32 sum of this unit's k-blocks (no bias)
       if (row < p.M)
