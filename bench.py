@@ -45,7 +45,7 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 # DRAM bytes (read + write) per projection launch of the c3 forward, mean of
 # the four projections of a layer, from one ncu capture of each shape (the
 # capture summaries are kept with the profiles)
-C3_GEMM_DRAM_BYTES_PER_LAUNCH = 147.9e6
+C3_GEMM_DRAM_BYTES_PER_LAUNCH = 150.9e6
 L2_FLUSH_BYTES = 256 << 20
 
 
