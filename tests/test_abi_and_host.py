@@ -122,3 +122,27 @@ def test_mask_resolution_memoised(monkeypatch):
     mask2[1, 100:] = False
     assert m._resolve_mask_active(mask2) is True
     assert m._resolve_mask_active(None) is False
+
+
+def test_splitk_choice():
+    """Few-row projections take the split-K form (fewer than a quarter of the
+    SMs would get a 128x64 tile, K >= 512); the c3-sized ones do not."""
+    from transformer_optimization_b200.model import _splitk
+    assert _splitk(64, 512, 2048, 148) == 0      # c2 FFN-out
+    assert _splitk(256, 256, 1024, 148) == 0     # c1 FFN-out
+    assert _splitk(256, 768, 256, 148) is None   # c1 QKV: K too short to split
+    assert _splitk(16384, 3072, 1024, 148) is None
+    assert _splitk(64, 512, 2048, 16) is None    # few SMs: enough tiles already
+
+
+def test_bench_algorithmic_bytes():
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("bench_mod", ROOT / "bench.py")
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    cfg = NAMED_CONFIGS["c3"]
+    m, d, f = 16384, 1024, 4096
+    expect = (2 * (m * d + 3 * d * d + 3 * m * d) + 2 * (m * d + f * d + m * f)
+              + 2 * (m * d + d * d) + 8 * m * d + 2 * (m * f + d * f) + 8 * m * d) / 4
+    assert bench.algo_bytes_per_gemm(cfg) == expect
+    assert 140e6 < bench.C3_GEMM_DRAM_BYTES_PER_LAUNCH < expect  # measured DRAM bytes below algorithmic
