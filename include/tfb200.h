@@ -18,7 +18,12 @@
  *     Kernels never trap: a pipeline wait that exceeds its time bound writes a
  *     code into the device status word (read with tf_device_status) and the
  *     kernel returns.
- *   - fp16 = IEEE binary16 ("half"), fp32 = binary32.
+ *   - fp16 = IEEE binary16 ("half"), bf16 = bfloat16, fp32 = binary32.
+ *   - Two model precisions: the fp32 model (fp16 tensor-core operands, fp32
+ *     residual stream and statistics: the reference's fp32-model fast path)
+ *     and the half-precision models (fp16 or bf16 parameters and
+ *     activations, type T below; every stored tensor is T as in the
+ *     reference's eager model run in T). Flags select the second.
  */
 #ifndef TFB200_H
 #define TFB200_H
@@ -45,16 +50,25 @@ extern "C" {
 #define TF_LN_MASK_OUT 4   /* zero invalid rows of the normalised output */
 #define TF_LN_WRITE_X 8    /* store the updated residual into x_out */
 #define TF_LN_OUT_F32 16   /* normed is fp32 (default fp16) */
+#define TF_LN_X_F16 32     /* x, delta, x_out and normed are fp16; x + delta is rounded to fp16 */
+#define TF_LN_X_BF16 64    /* x, delta, x_out and normed are bf16; x + delta is rounded to bf16 */
 
-/* tf_gemm epilogues (low bits) and options */
-#define TF_EPI_BIAS 0       /* C = fp16(acc + bias) */
-#define TF_EPI_BIAS_GELU 1  /* C = fp16(gelu_erf(acc + bias)), GELU in fp32 */
+/* tf_gemm epilogues (low bits) and options; T = the operand type */
+#define TF_EPI_BIAS 0       /* C = T(acc + bias) */
+#define TF_EPI_BIAS_GELU 1  /* C = T(gelu_erf(acc + bias)), GELU in fp32 */
+#define TF_EPI_BIAS_GELU_ROUNDED 2 /* C = T(gelu_erf(T(acc + bias))): F.gelu applied to the
+                                      stored T output of the Linear (half-precision models) */
 #define TF_EPI_W_SPLIT 16   /* W is [N, 2K] = [W_hi | W_lo] (W_lo = fp16(W - W_hi)) */
+#define TF_EPI_BF16 32      /* A, W and C are bf16 (default fp16) */
 
-/* tf_gemm_residual mask modes (the reference's two masking points) */
+/* tf_gemm_residual mask modes (the reference's two masking points), low 2 bits */
 #define TF_RES_NO_MASK 0
 #define TF_RES_MASK_DELTA 1 /* invalid rows: x_out = x_in (delta zeroed) */
 #define TF_RES_MASK_X 2     /* invalid rows: x_out = 0 */
+/* and options, or-ed into the mask mode */
+#define TF_RES_X16 4   /* x_in / x_out in the operand type T (default fp32):
+                          x_out = T(mask_x(x_in + mask_delta(T(acc + bias)))) */
+#define TF_RES_BF16 8  /* A and W (and x with TF_RES_X16) are bf16 (default fp16) */
 
 /* tf_flash_fwd flags */
 #define TF_ATTN_CAUSAL 1  /* mask key position > query position */
@@ -62,6 +76,8 @@ extern "C" {
 #define TF_ATTN_EXP_F16X2 4 /* packed fp16 exp2 for the probabilities (default:
                                fp32 exp2, the faster of the two on B200; P is
                                rounded to fp16 for the PV product either way) */
+#define TF_ATTN_BF16 8      /* q, k, v and out (unless TF_ATTN_OUT_F32) are bf16;
+                               P is rounded to bf16 for the PV product */
 /* flags bits 8..15: how many of the 64 probability pairs per row and key
  * block are exponentiated on the FMA pipes instead of the exp unit
  * (0, 8, 16 or 24; with TF_ATTN_EXP_F16X2: 0 or 16) */
@@ -82,20 +98,26 @@ int tf_device_status(int* code, void* stream);
 /* One residual-add + LayerNorm site over a contiguous [M, D] activation:
  *   x_new  = mask_x(x + mask_delta(fp32(delta)))
  *   normed = mask_out(LayerNorm(x_new) * w + b)       (fp16 or fp32 store)
- * delta is fp16 [M, D] or NULL (no add); valid is uint8 [M] (nonzero = valid
- * token) or NULL when no mask flag is set; x_out may alias nothing else and
- * is written only with TF_LN_WRITE_X. D must be a multiple of 8, <= 4096.
+ * x and x_out fp32, delta fp16 [M, D] or NULL (no add); with TF_LN_X_F16 /
+ * TF_LN_X_BF16 x, delta, x_out and normed are all that 16-bit type and
+ * x_new = T(x + delta) (statistics in fp32 either way). valid is uint8 [M]
+ * (nonzero = valid token) or NULL when no mask flag is set; x_out may alias
+ * nothing else and is written only with TF_LN_WRITE_X. w, b fp32. D must be
+ * a multiple of 8, <= 4096.
  * Replaces _ln_site / _triton_add_layernorm / _add_ln_kernel
- * (torch_transformer_benchmark.py:3940-4001, 1038-1108, 884-962). */
-int tf_ln_residual(const float* x, const void* delta, const float* w, const float* b, float eps,
-                   const uint8_t* valid, int64_t M, int64_t D, int flags, float* x_out, void* normed,
+ * (torch_transformer_benchmark.py:3940-4001, 1038-1108, 884-962) and, for
+ * half-precision models, `x + delta` followed by nn.LayerNorm
+ * (torch_transformer_benchmark.py:218-222, 245). */
+int tf_ln_residual(const void* x, const void* delta, const float* w, const float* b, float eps,
+                   const uint8_t* valid, int64_t M, int64_t D, int flags, void* x_out, void* normed,
                    void* stream);
 
-/* fp16 GEMM, fp32 accumulation on tcgen05 tensor cores:
+/* 16-bit GEMM, fp32 accumulation on tcgen05 tensor cores:
  *   C[M, N] = epilogue(A[M, K] * W[N, K]^T + bias[N])
  * A row-major with pitch lda, W = nn.Linear weight [N, K] (or [N, 2K] with
- * TF_EPI_W_SPLIT) with pitch ldw, C row-major with pitch ldc; A, W, C fp16,
- * bias fp32. N % 32 == 0, K and pitches % 8 == 0, pointers 16-byte aligned.
+ * TF_EPI_W_SPLIT) with pitch ldw, C row-major with pitch ldc; A, W, C fp16
+ * (bf16 with TF_EPI_BF16), bias fp32. N % 32 == 0, K and pitches % 8 == 0,
+ * pointers 16-byte aligned.
  * Replaces _lin / _triton_linear / _triton_gemm_gelu / F.linear on the
  * fp16-GEMM path (torch_transformer_benchmark.py:4138-4194, 1860-1906,
  * kernel 1756-1803). */
@@ -108,16 +130,19 @@ int tf_gemm(const void* A, int64_t lda, const void* W, int64_t ldw, const float*
 int tf_gemm_tiled(const void* A, int64_t lda, const void* W, int64_t ldw, const float* bias, void* C,
                   int64_t ldc, int64_t M, int64_t N, int64_t K, int epilogue, int tile_n, int pair, void* stream);
 
-/* GEMM whose epilogue closes a residual connection in fp32:
+/* GEMM whose epilogue closes a residual connection:
  *   x_out[M, N] = mask_x(x_in + mask_delta(A * W^T + bias))
  * x_in / x_out fp32 with pitch ldx (x_out may equal x_in: in place); valid
- * uint8 [M] for the mask modes. w_split != 0: W is [N, 2K] = [W_hi | W_lo].
+ * uint8 [M] for the mask modes. mask_mode may carry TF_RES_X16 (x in the
+ * operand type, with the half-precision model's two roundings) and
+ * TF_RES_BF16 (bf16 operands). w_split != 0: W is [N, 2K] = [W_hi | W_lo]
+ * (fp16 operands only).
  * tile_n / pair: tiling as in tf_gemm_tiled (0, 0 = automatic).
  * Replaces out_proj / ffn_out (torch_transformer_benchmark.py:4163-4169,
  * 4194) together with the residual add of the following _ln_site
  * (torch_transformer_benchmark.py:3988-3995). */
 int tf_gemm_residual(const void* A, int64_t lda, const void* W, int64_t ldw, const float* bias,
-                     const float* x_in, float* x_out, int64_t ldx, const uint8_t* valid, int mask_mode,
+                     const void* x_in, void* x_out, int64_t ldx, const uint8_t* valid, int mask_mode,
                      int64_t M, int64_t N, int64_t K, int w_split, int tile_n, int pair, void* stream);
 
 /* Split-K forms of tf_gemm / tf_gemm_residual for few-row inputs (small
@@ -136,7 +161,7 @@ int tf_gemm_splitk(const void* A, int64_t lda, const void* W, int64_t ldw, const
                    int64_t M, int64_t N, int64_t K, int epilogue, int splits, void* workspace,
                    int64_t workspace_bytes, void* stream);
 int tf_gemm_residual_splitk(const void* A, int64_t lda, const void* W, int64_t ldw, const float* bias,
-                            const float* x_in, float* x_out, int64_t ldx, const uint8_t* valid, int mask_mode,
+                            const void* x_in, void* x_out, int64_t ldx, const uint8_t* valid, int mask_mode,
                             int64_t M, int64_t N, int64_t K, int splits, void* workspace, int64_t workspace_bytes,
                             void* stream);
 
@@ -162,9 +187,10 @@ int tf_gemm_splitk_static(const void* A, int64_t lda, const void* W, int64_t ldw
 
 /* Flash attention forward (online softmax, no score matrix in HBM):
  *   out[b, i, h*hd:(h+1)*hd] = sum_j softmax_j(scale * q_i . k_j) v_j
- * q: fp16, token i of batch b, head h at q + b*bs_q + i*ld_q + h*hd;
- * k, v: same with ld_kv / bs_kv over seq_k tokens; out: fp16 (or fp32 with
- * TF_ATTN_OUT_F32) with ld_o / bs_o. lse: fp32 [batch, heads, seq_q] natural
+ * q: fp16 (bf16 with TF_ATTN_BF16), token i of batch b, head h at
+ * q + b*bs_q + i*ld_q + h*hd;
+ * k, v: same with ld_kv / bs_kv over seq_k tokens; out: q's type (or fp32
+ * with TF_ATTN_OUT_F32) with ld_o / bs_o. lse: fp32 [batch, heads, seq_q] natural
  * log-sum-exp of the scaled scores per row, or NULL. key_valid: uint8
  * [batch, seq_k] (nonzero = key may be attended) or NULL. With
  * TF_ATTN_CAUSAL key j is masked when k_pos0 + j > q_pos0 + i (positions

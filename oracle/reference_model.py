@@ -333,6 +333,60 @@ def linear_residual(a16: torch.Tensor, w: torch.Tensor, b: torch.Tensor, x_in: t
     return y.float()
 
 
+# Half-precision models (parameters and activations in T = fp16 or bf16): the
+# eager model run in T stores every op's output in T
+# (torch_transformer_benchmark.py:162-248 with T tensors). These restate the
+# roundings of one kernel call of that path, from exact (fp64) products.
+
+def ln_site_half(x: torch.Tensor, delta: Optional[torch.Tensor], w: torch.Tensor, b: torch.Tensor,
+                 eps: float, valid: Optional[torch.Tensor], mask_delta: bool, mask_x: bool,
+                 mask_out: bool, dtype: torch.dtype) -> Tuple[torch.Tensor, torch.Tensor]:
+    """`x = x + delta` stored in T (torch_transformer_benchmark.py:218-222),
+    then nn.LayerNorm of the T tensor (fp32 statistics, output rounded to T by
+    the caller's comparison), with the masking points of ln_site. x, delta in
+    T; returns fp32 (x_new with T values, normed before its rounding)."""
+    xf = x.float()
+    inv = None if valid is None else (~valid.reshape(-1, 1).bool())
+    if delta is not None:
+        d = delta.float()
+        if mask_delta:
+            d = d.masked_fill(inv, 0)
+        xf = (xf + d).to(dtype).float()
+    if mask_x:
+        xf = xf.masked_fill(inv, 0)
+    y = F.layer_norm(xf, (xf.shape[-1],), w.float(), b.float(), eps)
+    if mask_out:
+        y = y.masked_fill(inv, 0)
+    return xf, y
+
+
+def linear_half(a: torch.Tensor, w: torch.Tensor, b: torch.Tensor, gelu: bool,
+                dtype: torch.dtype) -> torch.Tensor:
+    """T(a @ w^T + b) from an exact (fp64) product, and with `gelu` the exact-
+    erf GELU of that stored T value, rounded to T again: nn.Linear then F.gelu
+    on T tensors (torch_transformer_benchmark.py:224). Returns fp32 values."""
+    h = (a.double() @ w.double().t() + b.double()).to(dtype)
+    if gelu:
+        h = F.gelu(h.double(), approximate="none").to(dtype)
+    return h.float()
+
+
+def linear_residual_half(a: torch.Tensor, w: torch.Tensor, b: torch.Tensor, x_in: torch.Tensor,
+                         valid: Optional[torch.Tensor], mask_delta: bool, mask_x: bool,
+                         dtype: torch.dtype) -> Tuple[torch.Tensor, torch.Tensor]:
+    """x = T(x + T(a @ w^T + b)) with the masking points of linear_residual:
+    the out_proj / ffn_out output stored in T, then the residual add stored in
+    T (torch_transformer_benchmark.py:197-200, 218-226). Returns fp32
+    (x_new, the stored projection)."""
+    v = (a.double() @ w.double().t() + b.double()).to(dtype).double()
+    if valid is not None and mask_delta:
+        v = v.masked_fill(~valid.reshape(-1, 1).bool(), 0)
+    y = (x_in.double() + v).to(dtype).double()
+    if valid is not None and mask_x:
+        y = y.masked_fill(~valid.reshape(-1, 1).bool(), 0)
+    return y.float(), v.float()
+
+
 def attention_fp16(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float,
                    causal: bool, key_valid: Optional[torch.Tensor] = None,
                    q_offset: int = 0) -> Tuple[torch.Tensor, torch.Tensor]:

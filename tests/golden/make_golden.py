@@ -17,6 +17,11 @@ runs the reference's own eager forward in fp32 on the CPU, and stores:
 
 The output file `golden_cases.pt` is small (<1 MB) and committed; the tests
 never need the reference checkout.
+
+`golden_half_cases.pt` holds the same records for half-precision models: the
+reference's model and input converted with `.to(dtype)` (fp16 or bf16, as the
+harness converts both before the accuracy check) and its eager forward run in
+that type on the CPU.
 """
 
 from __future__ import annotations
@@ -41,6 +46,16 @@ CASES = {
     "qtiled_causal": (1, 300, 128, 2, 256, 2, True, 0.0, 64, 5),
     "c1": (2, 128, 256, 4, 1024, 2, False, 0.0, None, 0),
     "c1_causal": (2, 128, 256, 4, 1024, 2, True, 0.0, None, 0),
+}
+
+# name: (B, S, D, H, F, L, causal, padding_ratio, seed, dtype)
+HALF_CASES = {
+    "tiny_fp16": (2, 32, 64, 2, 128, 2, False, 0.0, 0, torch.float16),
+    "tiny_causal_bf16": (2, 32, 64, 2, 128, 2, True, 0.0, 0, torch.bfloat16),
+    "tiny_padded_fp16": (3, 40, 64, 4, 96, 2, False, 0.4, 7, torch.float16),
+    "tiny_padded_causal_bf16": (3, 40, 64, 4, 96, 2, True, 0.4, 7, torch.bfloat16),
+    "c1_fp16": (2, 128, 256, 4, 1024, 2, False, 0.0, 0, torch.float16),
+    "c1_bf16": (2, 128, 256, 4, 1024, 2, False, 0.0, 0, torch.bfloat16),
 }
 
 FULL_LIMIT = 20000  # store the whole output below this many elements
@@ -98,6 +113,32 @@ def main(ref_root: str) -> None:
         out["cases"][name] = rec
         print(name, tuple(y.shape), float(y.double().sum()))
     torch.save(out, HERE / "golden_cases.pt")
+
+    half = {"torch_version": torch.__version__, "cases": {}}
+    for name, (b, s, d, h, f, l, causal, pad, seed, dtype) in HALF_CASES.items():
+        cfg = ttb.TransformerConfig(b, s, d, h, f, l, causal)
+        torch.manual_seed(seed)
+        model = ttb.BaselineTransformer(cfg)
+        x = torch.randn(b, s, d)
+        mask = padded_mask(cfg, pad, seed + 1000) if pad > 0 else None
+        if mask is not None:
+            x = x.masked_fill(~mask[..., None], 0)
+        sd32 = sd_checksum(model.state_dict())
+        model = model.to(dtype).eval()
+        xt = x.to(dtype)
+        with torch.inference_mode():
+            y = model(xt, mask)
+        assert y.dtype == dtype
+        rec = {"shape": (b, s, d, h, f, l, causal, pad, seed), "dtype": dtype, "sd_checksum": sd32,
+               "mask": mask}
+        if y.numel() <= FULL_LIMIT:
+            rec["y"], rec["y_index"] = y.clone(), None
+        else:
+            idx = torch.arange(0, s, 9)
+            rec["y"], rec["y_index"] = y[:, idx, :].clone(), idx
+        half["cases"][name] = rec
+        print(name, tuple(y.shape), float(y.double().sum()))
+    torch.save(half, HERE / "golden_half_cases.pt")
 
 
 if __name__ == "__main__":

@@ -1,0 +1,117 @@
+"""fp16 and bf16 models end to end on a B200: UserOptimizedTransformer with
+parameters and input in T (model.to(T), x.to(T)) against the eager model run
+in T on the GPU - the oracle's forward on T tensors, i.e. the ATen ops of the
+reference's BaselineTransformer (torch_transformer_benchmark.py:135-248) in
+that type - and against the fp32 model on the same T-valued weights and
+input (TF32 off), which both T results approximate.
+
+Gates:
+* fp16: the reference's own gate (compare_outputs, |d| <= 0.002 OR
+  |d| <= 0.02*|ref|, zero failing elements) against the eager fp16 model.
+* bf16: the same gate with both thresholds scaled by the resolution ratio of
+  bf16 to fp16 (2^-7 / 2^-10 = 8: |d| <= 0.016 OR |d| <= 0.16*|ref|). Two
+  correct bf16 computations that round in a different order differ by a few
+  bf16 ulps (0.0039 at magnitude 0.5), which the fp16-calibrated thresholds
+  cannot absorb; the reference passes its gate there only by calling the same
+  ATen kernels as its baseline.
+* both types: no less accurate than the eager model in T: against the fp32
+  model, mean |error| <= 1.02x and max |error| <= 1.25x the eager model's.
+"""
+
+import pytest
+import torch
+
+from oracle import reference_model as om
+from transformer_optimization_b200 import NAMED_CONFIGS, TransformerConfig, UserOptimizedTransformer
+
+pytestmark = pytest.mark.gpu
+
+CONFIGS = {
+    "c1": NAMED_CONFIGS["c1"],
+    "c1_causal": TransformerConfig(2, 128, 256, 4, 1024, 2, True),
+    "c2": NAMED_CONFIGS["c2"],
+    "ragged_hd128": TransformerConfig(1, 100, 256, 2, 512, 1, False),
+    "ragged_causal": TransformerConfig(3, 300, 128, 2, 256, 2, True),
+    "d2048_hd128": TransformerConfig(2, 256, 2048, 16, 8192, 2, False),
+    "c3_2layers": TransformerConfig(8, 2048, 1024, 16, 4096, 2, False),
+}
+GATE = {torch.float16: (0.002, 0.02), torch.bfloat16: (0.016, 0.16)}
+
+
+@pytest.fixture(scope="module", autouse=True)
+def strict_fp32():
+    old = torch.backends.cuda.matmul.allow_tf32, torch.backends.cudnn.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.backends.cudnn.allow_tf32 = False
+    yield
+    torch.backends.cuda.matmul.allow_tf32, torch.backends.cudnn.allow_tf32 = old
+
+
+def _name(t):
+    return "bf16" if t == torch.bfloat16 else "fp16"
+
+
+def _run(cfg, dt, seed=0, mask=None, zero_masked=False):
+    p, x = om.seeded_case(cfg, seed)
+    if zero_masked:
+        x = x.masked_fill(~mask[..., None], 0)
+    pt = {k: v.to(dt) for k, v in p.items()}
+    xt = x.to(dt)
+    model = UserOptimizedTransformer(cfg)
+    model.load_state_dict(p, strict=True)
+    model = model.cuda().to(dt).eval()
+    mg = None if mask is None else mask.cuda()
+    with torch.inference_mode():
+        out = model(xt.cuda(), mg)
+        eager = om.forward({k: v.cuda() for k, v in pt.items()}, cfg, xt.cuda(), mg)
+        f32 = om.forward({k: v.float().cuda() for k, v in pt.items()}, cfg, xt.float().cuda(), mg)
+    assert out.dtype == dt and out.shape == x.shape
+    return out.float(), eager.float(), f32
+
+
+def _check(out, eager, f32, dt):
+    atol, rtol = GATE[dt]
+    r = om.compare_outputs(eager.cpu(), out.cpu(), rtol=rtol, atol=atol)
+    assert r.passed, (f"{r.failed_elements}/{r.total_elements} failed, max_abs={r.max_abs_error:.3g} "
+                      f"at {r.worst_index} ref={r.reference_at_worst:.6g} opt={r.optimized_at_worst:.6g}")
+    e_ours = (out - f32).abs()
+    e_eager = (eager - f32).abs()
+    assert float(e_ours.mean()) <= 1.02 * float(e_eager.mean()) + 1e-7, (float(e_ours.mean()), float(e_eager.mean()))
+    assert float(e_ours.max()) <= 1.25 * float(e_eager.max()) + 1e-6, (float(e_ours.max()), float(e_eager.max()))
+
+
+@pytest.mark.parametrize("dt", [torch.float16, torch.bfloat16], ids=_name)
+@pytest.mark.parametrize("name", sorted(CONFIGS))
+def test_half_model(name, dt):
+    out, eager, f32 = _run(CONFIGS[name], dt)
+    _check(out, eager, f32, dt)
+
+
+@pytest.mark.parametrize("dt", [torch.float16, torch.bfloat16], ids=_name)
+@pytest.mark.parametrize("causal", [False, True])
+def test_half_model_partial_mask(dt, causal):
+    cfg = TransformerConfig(3, 200, 256, 4, 1024, 2, causal)
+    mask = om.padded_mask(cfg, 0.4, 1007)
+    out, eager, f32 = _run(cfg, dt, seed=7, mask=mask, zero_masked=True)
+    _check(out, eager, f32, dt)
+    assert torch.count_nonzero(out.cpu()[~mask]) == 0
+
+
+def test_half_model_dtype_mismatch_and_replay():
+    """x must have the parameters' dtype; graph replays of a half model are
+    bit-identical and leave the input untouched."""
+    cfg = NAMED_CONFIGS["c1"]
+    p, x = om.seeded_case(cfg)
+    model = UserOptimizedTransformer(cfg)
+    model.load_state_dict(p, strict=True)
+    model = model.cuda().to(torch.bfloat16).eval()
+    xg = x.cuda()
+    with pytest.raises(ValueError, match="dtype"):
+        model(xg)  # fp32 input into a bf16 model
+    xb = xg.bfloat16()
+    keep = xb.clone()
+    with torch.inference_mode():
+        a = model(xb)
+        b = model(xb)
+    assert torch.equal(a, b) and torch.equal(xb, keep)
+    assert a.data_ptr() != b.data_ptr()

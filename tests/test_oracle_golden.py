@@ -54,6 +54,36 @@ def test_oracle_matches_reference(name):
     assert torch.allclose(y, rec["y"], rtol=0, atol=tol), (y - rec["y"]).abs().max()
 
 
+GOLDEN_HALF = torch.load(Path(__file__).parent / "golden" / "golden_half_cases.pt", weights_only=False)
+
+
+@pytest.mark.parametrize("name", sorted(GOLDEN_HALF["cases"]))
+def test_oracle_half_matches_reference(name):
+    """The oracle's forward on fp16 / bf16 parameters and input reproduces the
+    reference's eager model converted with .to(dtype): bit-equal on the torch
+    build that made the fixture, within a few ulps of the type otherwise."""
+    rec = GOLDEN_HALF["cases"][name]
+    b, s, d, h, f, l, causal, pad, seed = rec["shape"]
+    dt = rec["dtype"]
+    cfg = TransformerConfig(b, s, d, h, f, l, causal)
+    torch.set_num_threads(min(8, torch.get_num_threads()))
+    p, x = om.seeded_case(cfg, seed)
+    assert torch.allclose(_sd_checksum(p), rec["sd_checksum"], rtol=0, atol=1e-9)
+    mask = rec["mask"]
+    if mask is not None:
+        x = x.masked_fill(~mask[..., None], 0)
+    with torch.inference_mode():
+        y = om.forward({k: v.to(dt) for k, v in p.items()}, cfg, x.to(dt), mask)
+    assert y.dtype == dt
+    if rec["y_index"] is not None:
+        y = y[:, rec["y_index"], :]
+    if GOLDEN_HALF["torch_version"] == torch.__version__:
+        assert torch.equal(y, rec["y"])
+    else:
+        ulp = 2.0 ** -10 if dt == torch.float16 else 2.0 ** -7
+        assert torch.allclose(y.float(), rec["y"].float(), rtol=4 * ulp, atol=4 * ulp)
+
+
 def test_compare_outputs_or_criterion():
     """compare_outputs uses (abs<=atol) OR (abs<=rtol*|ref|), not isclose."""
     ref = torch.tensor([1.0, 0.1, 0.0, float("nan")])

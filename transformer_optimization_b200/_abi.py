@@ -30,18 +30,25 @@ TF_LN_MASK_X = 2
 TF_LN_MASK_OUT = 4
 TF_LN_WRITE_X = 8
 TF_LN_OUT_F32 = 16
+TF_LN_X_F16 = 32
+TF_LN_X_BF16 = 64
 
 TF_EPI_BIAS = 0
 TF_EPI_BIAS_GELU = 1
+TF_EPI_BIAS_GELU_ROUNDED = 2
 TF_EPI_W_SPLIT = 16
+TF_EPI_BF16 = 32
 
 TF_RES_NO_MASK = 0
 TF_RES_MASK_DELTA = 1
 TF_RES_MASK_X = 2
+TF_RES_X16 = 4
+TF_RES_BF16 = 8
 
 TF_ATTN_CAUSAL = 1
 TF_ATTN_OUT_F32 = 2
 TF_ATTN_EXP_F16X2 = 4
+TF_ATTN_BF16 = 8
 
 # every symbol include/tfb200.h declares, with its ctypes signature
 _P = ctypes.c_void_p

@@ -148,6 +148,8 @@ class ContextParallelTransformer:
         cfg = m.config
         if not x_local.is_cuda:
             raise RuntimeError("ContextParallelTransformer needs CUDA tensors (no CPU path)")
+        if x_local.dtype != torch.float32 or m.final_norm.weight.dtype != torch.float32:
+            raise NotImplementedError("context parallelism runs the fp32 model (fp32 ring merge)")
         x_local = x_local.contiguous()
         b, s_loc, d = x_local.shape
         if bounds is None:
@@ -177,12 +179,12 @@ class ContextParallelTransformer:
         cur = x_local
         for li, blk in enumerate(m.layers):
             w = wts[li]
-            kernels.ln_residual(cur, None, blk.norm1.weight, blk.norm1.bias, blk.norm1.eps, normed=normed)
+            kernels.ln_residual(cur, None, w.n1w, w.n1b, blk.norm1.eps, normed=normed)
             kernels.linear(normed, w.wqkv, w.bqkv, out=qkv)
             self.ring(qkv[..., :d], qkv[..., d:2 * d], qkv[..., 2 * d:], h, scale, cfg.causal, bounds, ctx,
                       mask_full)
             cur = kernels.linear_residual(ctx, w.wo, w.bo, cur, x_res, vflat, mask_delta=active)
-            kernels.ln_residual(cur, None, blk.norm2.weight, blk.norm2.bias, blk.norm2.eps, normed=normed)
+            kernels.ln_residual(cur, None, w.n2w, w.n2b, blk.norm2.eps, normed=normed)
             kernels.linear(normed, w.w1, w.b1, gelu=True, out=hidden)
             kernels.linear_residual(hidden, w.w2, w.b2, cur, x_res, vflat, mask_x=active, w_split=w.split_w2)
         fn = m.final_norm

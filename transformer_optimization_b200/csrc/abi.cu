@@ -166,7 +166,7 @@ static inline int begin_call() {
 
 extern "C" {
 
-int tf_abi_version(void) { return 7; }
+int tf_abi_version(void) { return 8; }
 
 const char* tf_last_error(void) { return tfb::g_msg; }
 
@@ -186,8 +186,8 @@ int tf_device_status(int* code, void* stream) {
   return host == 0 ? TF_OK : set_error(TF_ERR_TIMEOUT, "a kernel wait ran out (device code %d)", host);
 }
 
-int tf_ln_residual(const float* x, const void* delta, const float* w, const float* b, float eps,
-                   const uint8_t* valid, int64_t M, int64_t D, int flags, float* x_out, void* normed,
+int tf_ln_residual(const void* x, const void* delta, const float* w, const float* b, float eps,
+                   const uint8_t* valid, int64_t M, int64_t D, int flags, void* x_out, void* normed,
                    void* stream) {
   int rc = begin_call();
   if (rc) return rc;
@@ -196,10 +196,39 @@ int tf_ln_residual(const float* x, const void* delta, const float* w, const floa
                           as_stream(stream));
 }
 
+// Internal epilogue code and operand type of a tf_gemm* epilogue argument
+// (TF_EPI_BIAS, TF_EPI_BIAS_GELU or TF_EPI_BIAS_GELU_ROUNDED, optionally
+// with TF_EPI_BF16); -1 if it names none of them.
+static int gemm_epilogue(int epilogue, int& dtype) {
+  dtype = (epilogue & TF_EPI_BF16) ? tfb::kDtBF16 : tfb::kDtF16;
+  switch (epilogue & 0xF) {
+    case TF_EPI_BIAS: return 0;
+    case TF_EPI_BIAS_GELU: return 1;
+    case TF_EPI_BIAS_GELU_ROUNDED: return 5;
+    default: return -1;
+  }
+}
+
+// Internal residual epilogue, mask mode and operand type of a
+// tf_gemm_residual* mask_mode argument; false if it is malformed.
+static bool residual_mode(int mask_mode, int& epi, int& mask, int& dtype) {
+  if (mask_mode & ~(3 | TF_RES_X16 | TF_RES_BF16)) return false;
+  mask = mask_mode & 3;
+  if (mask > 2) return false;
+  epi = (mask_mode & TF_RES_X16) ? 4 : 2;
+  dtype = (mask_mode & TF_RES_BF16) ? tfb::kDtBF16 : tfb::kDtF16;
+  return true;
+}
+
 static int gemm_common(const void* A, int64_t lda, const void* W, int64_t ldw, const float* bias, void* C,
                        int64_t ldc, int64_t M, int64_t N, int64_t K, int epilogue, int tile_n, int pair,
                        void* stream) {
-  if (epilogue & ~(0xF | TF_EPI_W_SPLIT)) return set_error(TF_ERR_SHAPE, "tf_gemm: unknown epilogue bits");
+  if (epilogue & ~(0xF | TF_EPI_W_SPLIT | TF_EPI_BF16)) return set_error(TF_ERR_SHAPE, "tf_gemm: unknown epilogue bits");
+  int dtype = 0;
+  const int epi = gemm_epilogue(epilogue, dtype);
+  if (epi < 0) return set_error(TF_ERR_SHAPE, "tf_gemm: epilogue %d", epilogue & 0xF);
+  if ((epilogue & TF_EPI_W_SPLIT) && dtype != tfb::kDtF16)
+    return set_error(TF_ERR_SHAPE, "tf_gemm: split weights are fp16 only");
   tfb::GemmCall g = {};
   g.A = A;
   g.lda = lda;
@@ -211,8 +240,8 @@ static int gemm_common(const void* A, int64_t lda, const void* W, int64_t ldw, c
   g.M = M;
   g.N = N;
   g.K = K;
-  g.epilogue = epilogue & 0xF;
-  if (g.epilogue > 1) return set_error(TF_ERR_SHAPE, "tf_gemm: epilogue %d", g.epilogue);
+  g.epilogue = epi;
+  g.dtype = dtype;
   g.a_repeat = (epilogue & TF_EPI_W_SPLIT) ? 2 : 1;
   g.tile_n = tile_n;
   g.pair = pair;
@@ -239,10 +268,14 @@ int tf_gemm_tiled(const void* A, int64_t lda, const void* W, int64_t ldw, const 
 }
 
 int tf_gemm_residual(const void* A, int64_t lda, const void* W, int64_t ldw, const float* bias,
-                     const float* x_in, float* x_out, int64_t ldx, const uint8_t* valid, int mask_mode,
+                     const void* x_in, void* x_out, int64_t ldx, const uint8_t* valid, int mask_mode,
                      int64_t M, int64_t N, int64_t K, int w_split, int tile_n, int pair, void* stream) {
   int rc = begin_call();
   if (rc) return rc;
+  int epi = 0, mask = 0, dtype = 0;
+  if (!residual_mode(mask_mode, epi, mask, dtype))
+    return set_error(TF_ERR_SHAPE, "tf_gemm_residual: mask_mode=%d", mask_mode);
+  if (w_split && dtype != tfb::kDtF16) return set_error(TF_ERR_SHAPE, "tf_gemm_residual: split weights are fp16 only");
   if (tile_n != 0 && tile_n != 64 && tile_n != 128 && tile_n != 256)
     return set_error(TF_ERR_SHAPE, "tf_gemm_residual: tile_n=%d (0, 64, 128 or 256)", tile_n);
   if (pair < 0 || pair > 2 || (pair == 2 && tile_n == 64))
@@ -257,11 +290,12 @@ int tf_gemm_residual(const void* A, int64_t lda, const void* W, int64_t ldw, con
   g.x_out = x_out;
   g.ldx = ldx;
   g.valid = valid;
-  g.mask_mode = mask_mode;
+  g.mask_mode = mask;
   g.M = M;
   g.N = N;
   g.K = K;
-  g.epilogue = 2;
+  g.epilogue = epi;
+  g.dtype = dtype;
   g.a_repeat = w_split ? 2 : 1;
   g.tile_n = tile_n;
   g.pair = pair;
@@ -278,8 +312,9 @@ int tf_gemm_splitk(const void* A, int64_t lda, const void* W, int64_t ldw, const
                    int64_t workspace_bytes, void* stream) {
   int rc = begin_call();
   if (rc) return rc;
-  if (epilogue != TF_EPI_BIAS && epilogue != TF_EPI_BIAS_GELU)
-    return set_error(TF_ERR_SHAPE, "tf_gemm_splitk: epilogue=%d (TF_EPI_BIAS or TF_EPI_BIAS_GELU)", epilogue);
+  int dtype = 0;
+  const int epi = (epilogue & ~(0xF | TF_EPI_BF16)) ? -1 : gemm_epilogue(epilogue, dtype);
+  if (epi < 0) return set_error(TF_ERR_SHAPE, "tf_gemm_splitk: epilogue=%d", epilogue);
   tfb::GemmCall g = {};
   g.A = A;
   g.lda = lda;
@@ -291,7 +326,8 @@ int tf_gemm_splitk(const void* A, int64_t lda, const void* W, int64_t ldw, const
   g.M = M;
   g.N = N;
   g.K = K;
-  g.epilogue = epilogue;
+  g.epilogue = epi;
+  g.dtype = dtype;
   g.a_repeat = 1;
   return tfb::gemm_splitk_f16(g, splits, static_cast<float*>(workspace), workspace_bytes, as_stream(stream));
 }
@@ -300,8 +336,9 @@ int tf_gemm_splitk_static(const void* A, int64_t lda, const void* W, int64_t ldw
                           int64_t ldc, int64_t M, int64_t N, int64_t K, int epilogue, int splits, void* stream) {
   int rc = begin_call();
   if (rc) return rc;
-  if (epilogue != TF_EPI_BIAS && epilogue != TF_EPI_BIAS_GELU)
-    return set_error(TF_ERR_SHAPE, "tf_gemm_splitk_static: epilogue=%d (TF_EPI_BIAS or TF_EPI_BIAS_GELU)", epilogue);
+  int dtype = 0;
+  const int epi = (epilogue & ~(0xF | TF_EPI_BF16)) ? -1 : gemm_epilogue(epilogue, dtype);
+  if (epi < 0) return set_error(TF_ERR_SHAPE, "tf_gemm_splitk_static: epilogue=%d", epilogue);
   tfb::GemmCall g = {};
   g.A = A;
   g.lda = lda;
@@ -313,18 +350,21 @@ int tf_gemm_splitk_static(const void* A, int64_t lda, const void* W, int64_t ldw
   g.M = M;
   g.N = N;
   g.K = K;
-  g.epilogue = epilogue;
+  g.epilogue = epi;
+  g.dtype = dtype;
   g.a_repeat = 1;
   return tfb::gemm_splitk_static_f16(g, splits, as_stream(stream));
 }
 
 int tf_gemm_residual_splitk(const void* A, int64_t lda, const void* W, int64_t ldw, const float* bias,
-                            const float* x_in, float* x_out, int64_t ldx, const uint8_t* valid, int mask_mode,
+                            const void* x_in, void* x_out, int64_t ldx, const uint8_t* valid, int mask_mode,
                             int64_t M, int64_t N, int64_t K, int splits, void* workspace, int64_t workspace_bytes,
                             void* stream) {
   int rc = begin_call();
   if (rc) return rc;
-  if (mask_mode < 0 || mask_mode > 2) return set_error(TF_ERR_SHAPE, "tf_gemm_residual_splitk: mask_mode=%d", mask_mode);
+  int epi = 0, mask = 0, dtype = 0;
+  if (!residual_mode(mask_mode, epi, mask, dtype))
+    return set_error(TF_ERR_SHAPE, "tf_gemm_residual_splitk: mask_mode=%d", mask_mode);
   tfb::GemmCall g = {};
   g.A = A;
   g.lda = lda;
@@ -335,11 +375,12 @@ int tf_gemm_residual_splitk(const void* A, int64_t lda, const void* W, int64_t l
   g.x_out = x_out;
   g.ldx = ldx;
   g.valid = valid;
-  g.mask_mode = mask_mode;
+  g.mask_mode = mask;
   g.M = M;
   g.N = N;
   g.K = K;
-  g.epilogue = 2;
+  g.epilogue = epi;
+  g.dtype = dtype;
   g.a_repeat = 1;
   return tfb::gemm_splitk_f16(g, splits, static_cast<float*>(workspace), workspace_bytes, as_stream(stream));
 }

@@ -9,9 +9,12 @@
 #pragma once
 
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+
+#include "launch.h"
 
 namespace tfb {
 
@@ -265,6 +268,13 @@ __host__ __device__ constexpr uint32_t idesc_f16_f32(int m, int n, bool a_mn = f
          | (static_cast<uint32_t>(m >> 4) << 24); // M / 16
 }
 
+// kind::f16 instruction descriptor for operands of type dt (kDtF16 or
+// kDtBF16): the A and B format fields (bits 7-9 and 10-12) are 0 for f16 and
+// 1 for bf16; in one MMA both operands have the same type.
+__host__ __device__ constexpr uint32_t idesc_16_f32(int dt, int m, int n, bool a_mn = false, bool b_mn = false) {
+  return idesc_f16_f32(m, n, a_mn, b_mn) | (dt == kDtBF16 ? ((1u << 7) | (1u << 10)) : 0u);
+}
+
 // ---------------------------------------------------------------------------
 // misc
 // ---------------------------------------------------------------------------
@@ -304,6 +314,37 @@ __device__ __forceinline__ float gelu_erf(float x) {
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
   __half2 h = __floats2half2_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Two floats rounded to nearest-even into a 16-bit pair of type DT (lo in the
+// low half), and back (exact).
+template <int DT>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  if constexpr (DT == kDtBF16) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+  } else {
+    return pack_half2(lo, hi);
+  }
+}
+
+template <int DT>
+__device__ __forceinline__ float2 unpack2(uint32_t v) {
+  if constexpr (DT == kDtBF16) {
+    return make_float2(__uint_as_float(v << 16), __uint_as_float(v & 0xffff0000u));
+  } else {
+    return __half22float2(*reinterpret_cast<const __half2*>(&v));
+  }
+}
+
+// x rounded to the 16-bit type DT (nearest-even) and widened back.
+template <int DT>
+__device__ __forceinline__ float round16(float x) {
+  if constexpr (DT == kDtBF16) {
+    return __bfloat162float(__float2bfloat16_rn(x));
+  } else {
+    return __half2float(__float2half_rn(x));
+  }
 }
 
 __device__ __forceinline__ int lane_id() { return threadIdx.x & 31; }

@@ -35,6 +35,10 @@
 //
 // The kernel also emits the natural-log sum-exp per row, used to merge the
 // partial results of context-parallel ring attention exactly.
+//
+// Operand type DT: fp16 (the fp32 model's compute type, and fp16 models) or
+// bf16 (bf16 models, whose eager attention rounds the probabilities to bf16
+// before P V: torch_transformer_benchmark.py:190-191); P is rounded to DT.
 #include "common.cuh"
 #include "launch.h"
 
@@ -165,6 +169,22 @@ __device__ __forceinline__ uint32_t pack_f16x2_rn(float a, float b) {
   return h;
 }
 
+__device__ __forceinline__ uint32_t pack_bf16x2_rn(float a, float b) {
+  uint32_t h;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(b), "f"(a));
+  return h;
+}
+
+// a probability pair in the PV operand type (a in the low half)
+template <int DT>
+__device__ __forceinline__ uint32_t pack_p(float a, float b) {
+  if constexpr (DT == kDtBF16) {
+    return pack_bf16x2_rn(a, b);
+  } else {
+    return pack_f16x2_rn(a, b);
+  }
+}
+
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
@@ -211,7 +231,7 @@ __device__ __forceinline__ void rescale_o(uint32_t taddr, float alpha) {
   tmem_wait_st();
 }
 
-template <int HD, bool EXP16, int POLY>
+template <int HD, bool EXP16, int POLY, int DT>
 __global__ void __launch_bounds__(kAttnThreads, 1)
     flash_fwd_tcgen05(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                       const __grid_constant__ CUtensorMap tmV, AttnKParams p) {
@@ -348,8 +368,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       // its own inputs, so neither stalls behind the other's barrier waits
       // and commits (the tensor core queue is shallow). A slot's next S
       // waits for the completion of the PV that read the slot's P (pv_done).
-      constexpr uint32_t idesc_s = idesc_f16_f32(kAttnBM, kAttnBN);     // K-major Q, K-major K
-      constexpr uint32_t idesc_o = idesc_f16_f32(kAttnBM, HD, false, true);  // K-major P, MN-major V
+      constexpr uint32_t idesc_s = idesc_16_f32(DT, kAttnBM, kAttnBN);     // K-major Q, K-major K
+      constexpr uint32_t idesc_o = idesc_16_f32(DT, kAttnBM, HD, false, true);  // K-major P, MN-major V
       const uint32_t sbase = smem_u32(smem);
       auto pair_of = [&](int q, int& t, int& j) {
         if (q < 2 * nmin) {
@@ -554,7 +574,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         for (int i = 0; i < 2 * POLY; ++i) s[i] = exp2_f32_fma(s[i]);
 #pragma unroll
         for (int i = 0; i < 64; ++i) {
-          pk[i] = pack_f16x2_rn(s[2 * i], s[2 * i + 1]);
+          pk[i] = pack_p<DT>(s[2 * i], s[2 * i + 1]);
           ls[i & 7] += s[2 * i] + s[2 * i + 1];
         }
       }
@@ -601,14 +621,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             dst[i] = make_float4(__uint_as_float(ov[4 * i]) * inv, __uint_as_float(ov[4 * i + 1]) * inv,
                                  __uint_as_float(ov[4 * i + 2]) * inv, __uint_as_float(ov[4 * i + 3]) * inv);
         } else {
-          uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(p.out) + obase);
+          uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.out) + obase);
 #pragma unroll
           for (int i = 0; i < HD / 8; ++i)
             dst[i] = make_uint4(
-                pack_half2(__uint_as_float(ov[8 * i]) * inv, __uint_as_float(ov[8 * i + 1]) * inv),
-                pack_half2(__uint_as_float(ov[8 * i + 2]) * inv, __uint_as_float(ov[8 * i + 3]) * inv),
-                pack_half2(__uint_as_float(ov[8 * i + 4]) * inv, __uint_as_float(ov[8 * i + 5]) * inv),
-                pack_half2(__uint_as_float(ov[8 * i + 6]) * inv, __uint_as_float(ov[8 * i + 7]) * inv));
+                pack2<DT>(__uint_as_float(ov[8 * i]) * inv, __uint_as_float(ov[8 * i + 1]) * inv),
+                pack2<DT>(__uint_as_float(ov[8 * i + 2]) * inv, __uint_as_float(ov[8 * i + 3]) * inv),
+                pack2<DT>(__uint_as_float(ov[8 * i + 4]) * inv, __uint_as_float(ov[8 * i + 5]) * inv),
+                pack2<DT>(__uint_as_float(ov[8 * i + 6]) * inv, __uint_as_float(ov[8 * i + 7]) * inv));
         }
       }
     }
@@ -659,11 +679,11 @@ __global__ void attn_merge_kernel(float* __restrict__ o_acc, float* __restrict__
 // host side
 // ---------------------------------------------------------------------------
 
-template <int HD, bool EXP16, int POLY>
+template <int HD, bool EXP16, int POLY, int DT = kDtF16>
 static int launch_flash(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                         const AttnKParams& kp, dim3 grid, cudaStream_t stream) {
   using C = AttnCfg<HD>;
-  auto kern = flash_fwd_tcgen05<HD, EXP16, POLY>;
+  auto kern = flash_fwd_tcgen05<HD, EXP16, POLY, DT>;
   static bool attr_done[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -738,6 +758,14 @@ int flash_fwd(const AttnArgs& a, cudaStream_t stream) {
     return set_error(TF_ERR_SHAPE, "flash: FMA-pipe exp pairs must be 0, 8, 16 or 24");
   if (exp16 && poly != 0 && poly != 16)
     return set_error(TF_ERR_SHAPE, "flash: with TF_ATTN_EXP_F16X2 the FMA-pipe exp pairs must be 0 or 16");
+  if (a.flags & TF_ATTN_BF16) {
+    // bf16 operands: fp32 exp2 on the exp unit only (the other exponential
+    // forms produce fp16 bits)
+    if (exp16 || poly != 0)
+      return set_error(TF_ERR_SHAPE, "flash: TF_ATTN_BF16 takes neither TF_ATTN_EXP_F16X2 nor FMA-pipe exponentials");
+    return a.head_dim == 64 ? launch_flash<64, false, 0, kDtBF16>(tq, tk, tv, kp, grid, stream)
+                            : launch_flash<128, false, 0, kDtBF16>(tq, tk, tv, kp, grid, stream);
+  }
 #define TFB_FLASH(E, P)                                                            \
   return a.head_dim == 64 ? launch_flash<64, E, P>(tq, tk, tv, kp, grid, stream) \
                           : launch_flash<128, E, P>(tq, tk, tv, kp, grid, stream);

@@ -12,6 +12,12 @@
 
 namespace tfb {
 
+// The two 16-bit operand types of the tensor-core kernels: kDtF16 (IEEE
+// binary16: the compute type of the fp32 model and the fp16 model's own type)
+// and kDtBF16 (bfloat16 models).
+constexpr int kDtF16 = 0;
+constexpr int kDtBF16 = 1;
+
 // Records a formatted message for tf_last_error() and returns `code`.
 int set_error(int code, const char* fmt, ...);
 int last_error_code();
@@ -66,29 +72,32 @@ struct GemmCall {
   const void* W;
   long long ldw;
   const float* bias;
-  void* C;  // fp16 output (epilogues 0, 1)
+  void* C;  // 16-bit output (epilogues 0, 1, 5)
   long long ldc;
-  const float* x_in;  // fp32 residual (epilogue 2)
-  float* x_out;
+  const void* x_in;  // residual: fp32 (epilogue 2) or the operand type (epilogue 4)
+  void* x_out;
   long long ldx;
   const uint8_t* valid;
   int mask_mode;
   long long M, N, K;
+  // 0 C = T(acc + bias); 1 C = T(gelu(acc + bias)); 2 fp32 residual add;
+  // 4 residual add in T; 5 C = T(gelu(T(acc + bias))). T = the operand type
   int epilogue;
+  int dtype;  // operand type: kDtF16 (0) or kDtBF16 (1)
   int a_repeat;
   int tile_n;
   int pair;  // 0 automatic, 1 one-CTA tiles, 2 two-SM (CTA pair) tiles
 };
 
 int gemm_f16(const GemmCall& g, cudaStream_t stream);
-// split-K GEMM (epilogues 0, 1, 2) with an fp32 partial-sum workspace
+// split-K GEMM (epilogues 0, 1, 2, 4, 5) with an fp32 partial-sum workspace
 int gemm_splitk_f16(const GemmCall& g, int splits, float* ws, long long ws_bytes, cudaStream_t stream);
 long long gemm_splitk_workspace_bytes(long long M, long long N, long long K, int splits);
 // the same with the library's fixed 4 MiB device scratch (no allocation)
 int gemm_splitk_static_f16(const GemmCall& g, int splits, cudaStream_t stream);
 
-int ln_residual(const float* x, const void* delta, const float* w, const float* b, float eps,
-                const uint8_t* valid, long long M, int D, int flags, float* x_out, void* normed,
+int ln_residual(const void* x, const void* delta, const float* w, const float* b, float eps,
+                const uint8_t* valid, long long M, int D, int flags, void* x_out, void* normed,
                 cudaStream_t stream);
 
 struct AttnArgs {

@@ -9,6 +9,11 @@
 // the two-pass moments over the row held in registers, as the reference
 // kernel does (mean first, then the centred sum of squares).
 //
+// Half-precision models (XT = kLnF16 / kLnBF16): x, delta and x_out are in the
+// model's type T and the sum is rounded to T before the statistics, as the
+// eager model stores `x = x + delta` in T before nn.LayerNorm reads it
+// (torch_transformer_benchmark.py:218-222); normed is T (or fp32).
+//
 // HBM-bound: bytes per row = D*(4 read x + 2 read delta + 4 write x + 2 write
 // normed). Two kernels:
 //  * ln_stream_kernel (D <= 2048): one persistent CTA per SM streams groups of
@@ -26,14 +31,34 @@ namespace tfb {
 
 constexpr int kLnRowsPerBlock = 8;
 
-template <int NCH>  // 8-element chunks per lane (row width up to 256*NCH)
-__global__ void __launch_bounds__(256) ln_residual_kernel(const float* __restrict__ x,
-                                                          const __half* __restrict__ delta,
+// Element type of the residual stream x (and of delta and x_out): the fp32
+// model keeps x in fp32 with an fp16 delta; the half-precision models keep
+// all three in their own 16-bit type.
+constexpr int kLnF32 = 0;
+constexpr int kLnF16 = 1;
+constexpr int kLnBF16 = 2;
+template <int XT>
+constexpr int kLnDt = XT == kLnBF16 ? kDtBF16 : kDtF16;  // type of delta and of a 16-bit normed
+
+// Four consecutive elements of a 16-bit row of type DT, widened.
+template <int DT>
+__device__ __forceinline__ void widen4(uint2 q, float (&v)[4]) {
+  const float2 a = unpack2<DT>(q.x), b = unpack2<DT>(q.y);
+  v[0] = a.x;
+  v[1] = a.y;
+  v[2] = b.x;
+  v[3] = b.y;
+}
+
+template <int NCH, int XT>  // 8-element chunks per lane (row width up to 256*NCH); x's type
+__global__ void __launch_bounds__(256) ln_residual_kernel(const void* __restrict__ x,
+                                                          const uint16_t* __restrict__ delta,
                                                           const float* __restrict__ w,
                                                           const float* __restrict__ b, float eps,
                                                           const uint8_t* __restrict__ valid, long long M, int D,
-                                                          int flags, float* __restrict__ x_out,
+                                                          int flags, void* __restrict__ x_out,
                                                           void* __restrict__ normed) {
+  constexpr int DT = kLnDt<XT>;
   pdl_wait();
   pdl_trigger();
   const int lane = threadIdx.x & 31;
@@ -41,7 +66,6 @@ __global__ void __launch_bounds__(256) ln_residual_kernel(const float* __restric
   for (long long row = static_cast<long long>(blockIdx.x) * kLnRowsPerBlock + (threadIdx.x >> 5); row < M;
        row += warps_total) {
   const int nchunk = D >> 3;
-  const float* xr = x + row * D;
   bool row_valid = true;
   if (valid != nullptr) row_valid = valid[row] != 0;
 
@@ -51,19 +75,35 @@ __global__ void __launch_bounds__(256) ln_residual_kernel(const float* __restric
   for (int i = 0; i < NCH; ++i) {
     const int c = lane + 32 * i;
     if (c < nchunk) {
-      const float4 a0 = __ldcs(reinterpret_cast<const float4*>(xr) + 2 * c);
-      const float4 a1 = __ldcs(reinterpret_cast<const float4*>(xr) + 2 * c + 1);
-      v[i][0] = a0.x; v[i][1] = a0.y; v[i][2] = a0.z; v[i][3] = a0.w;
-      v[i][4] = a1.x; v[i][5] = a1.y; v[i][6] = a1.z; v[i][7] = a1.w;
+      if constexpr (XT == kLnF32) {
+        const float* xr = static_cast<const float*>(x) + row * D;
+        const float4 a0 = __ldcs(reinterpret_cast<const float4*>(xr) + 2 * c);
+        const float4 a1 = __ldcs(reinterpret_cast<const float4*>(xr) + 2 * c + 1);
+        v[i][0] = a0.x; v[i][1] = a0.y; v[i][2] = a0.z; v[i][3] = a0.w;
+        v[i][4] = a1.x; v[i][5] = a1.y; v[i][6] = a1.z; v[i][7] = a1.w;
+      } else {
+        const uint4 q = __ldcs(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(x) + row * D) + c);
+        const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = unpack2<DT>(qw[j]);
+          v[i][2 * j] = f.x;
+          v[i][2 * j + 1] = f.y;
+        }
+      }
       if (delta != nullptr) {
         const uint4 dq = __ldcs(reinterpret_cast<const uint4*>(delta + row * D) + c);
-        const __half2* dh = reinterpret_cast<const __half2*>(&dq);
+        const uint32_t dw[4] = {dq.x, dq.y, dq.z, dq.w};
         const bool keep = !(flags & TF_LN_MASK_DELTA) || row_valid;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          const float2 f = __half22float2(dh[j]);
+          const float2 f = unpack2<DT>(dw[j]);
           v[i][2 * j] += keep ? f.x : 0.f;
           v[i][2 * j + 1] += keep ? f.y : 0.f;
+        }
+        if constexpr (XT != kLnF32) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) v[i][j] = round16<DT>(v[i][j]);
         }
       }
       if ((flags & TF_LN_MASK_X) && !row_valid) {
@@ -99,9 +139,15 @@ __global__ void __launch_bounds__(256) ln_residual_kernel(const float* __restric
     const int c = lane + 32 * i;
     if (c < nchunk) {
       if (flags & TF_LN_WRITE_X) {
-        float4* xo = reinterpret_cast<float4*>(x_out + row * D) + 2 * c;
-        __stcs(xo, make_float4(v[i][0], v[i][1], v[i][2], v[i][3]));
-        __stcs(xo + 1, make_float4(v[i][4], v[i][5], v[i][6], v[i][7]));
+        if constexpr (XT == kLnF32) {
+          float4* xo = reinterpret_cast<float4*>(static_cast<float*>(x_out) + row * D) + 2 * c;
+          __stcs(xo, make_float4(v[i][0], v[i][1], v[i][2], v[i][3]));
+          __stcs(xo + 1, make_float4(v[i][4], v[i][5], v[i][6], v[i][7]));
+        } else {
+          __stcs(reinterpret_cast<uint4*>(static_cast<uint16_t*>(x_out) + row * D) + c,
+                 make_uint4(pack2<DT>(v[i][0], v[i][1]), pack2<DT>(v[i][2], v[i][3]), pack2<DT>(v[i][4], v[i][5]),
+                            pack2<DT>(v[i][6], v[i][7])));
+        }
       }
       const float4 w0 = __ldg(reinterpret_cast<const float4*>(w) + 2 * c);
       const float4 w1 = __ldg(reinterpret_cast<const float4*>(w) + 2 * c + 1);
@@ -118,11 +164,11 @@ __global__ void __launch_bounds__(256) ln_residual_kernel(const float* __restric
         __stcs(no + 1, make_float4(y[4], y[5], y[6], y[7]));
       } else {
         uint4 q;
-        q.x = pack_half2(y[0], y[1]);
-        q.y = pack_half2(y[2], y[3]);
-        q.z = pack_half2(y[4], y[5]);
-        q.w = pack_half2(y[6], y[7]);
-        reinterpret_cast<uint4*>(static_cast<__half*>(normed) + row * D)[c] = q;
+        q.x = pack2<DT>(y[0], y[1]);
+        q.y = pack2<DT>(y[2], y[3]);
+        q.z = pack2<DT>(y[4], y[5]);
+        q.w = pack2<DT>(y[6], y[7]);
+        reinterpret_cast<uint4*>(static_cast<uint16_t*>(normed) + row * D)[c] = q;
       }
     }
   }
@@ -140,12 +186,12 @@ __host__ __device__ constexpr int lns_threads(int teams) { return 32 * (kLnsRows
 constexpr int kLnsSmemBudget = 196608;
 
 struct LnsParams {
-  const float* x;
-  const __half* delta;
+  const void* x;
+  const uint16_t* delta;
   const float* w;
   const float* b;
   const uint8_t* valid;
-  float* x_out;
+  void* x_out;
   void* normed;
   long long M;
   int D, flags, stages;
@@ -158,13 +204,15 @@ struct LnsParams {
 // TEAMS, so every stage is only ever used by one team, whose waits on it come
 // in phase order: an mbarrier waiter that could fall two phases behind would
 // see the parity of an older phase and read a stage that is being refilled.
-template <int NV, int TEAMS>  // NV: float4 per lane (row width up to 128*NV)
+template <int NV, int TEAMS, int XT>  // NV: 4-element vectors per lane (row width up to 128*NV); x's type
 __global__ void __launch_bounds__(lns_threads(TEAMS), 1) ln_stream_kernel(const LnsParams p) {
+  constexpr int DT = kLnDt<XT>;
+  constexpr int XS = XT == kLnF32 ? 4 : 2;  // bytes per x element
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
   const int D = p.D;
   const bool has_delta = p.delta != nullptr;
-  const uint32_t x_bytes = static_cast<uint32_t>(kLnsRows) * D * 4;
+  const uint32_t x_bytes = static_cast<uint32_t>(kLnsRows) * D * XS;
   const uint32_t stage_bytes = x_bytes + (has_delta ? static_cast<uint32_t>(kLnsRows) * D * 2 : 0u);
   // LayerNorm weight and bias staged once per CTA (read by every row)
   float* w_s = reinterpret_cast<float*>(smem + p.stages * stage_bytes);
@@ -202,10 +250,10 @@ __global__ void __launch_bounds__(lns_threads(TEAMS), 1) ln_stream_kernel(const 
         const long long r0 = g * kLnsRows;
         const int nrows = static_cast<int>(p.M - r0 < kLnsRows ? p.M - r0 : kLnsRows);
         uint8_t* st = smem + s * stage_bytes;
-        const uint32_t xb = static_cast<uint32_t>(nrows) * D * 4;
+        const uint32_t xb = static_cast<uint32_t>(nrows) * D * XS;
         const uint32_t db = has_delta ? static_cast<uint32_t>(nrows) * D * 2 : 0u;
         mbar_arrive_expect_tx(&full[s], xb + db);
-        bulk_load_1d(st, p.x + r0 * D, xb, &full[s]);
+        bulk_load_1d(st, static_cast<const uint8_t*>(p.x) + r0 * D * XS, xb, &full[s]);
         if (has_delta) bulk_load_1d(st + x_bytes, p.delta + r0 * D, db, &full[s]);
       }
     }
@@ -215,7 +263,7 @@ __global__ void __launch_bounds__(lns_threads(TEAMS), 1) ln_stream_kernel(const 
   // ---------------- consumers ----------------
   // team k = warp / 8 takes this CTA's groups k, k+TEAMS, ...; warp w of the
   // team takes row w % 8 of each
-  const int nv = D >> 2;  // float4 per row
+  const int nv = D >> 2;  // 4-element vectors per row
   const int team = warp / kLnsRows, wr = warp % kLnsRows;
   int it = team;
   for (long long g = blockIdx.x + static_cast<long long>(team) * gridDim.x; g < groups;
@@ -227,7 +275,7 @@ __global__ void __launch_bounds__(lns_threads(TEAMS), 1) ln_stream_kernel(const 
     if (p.valid != nullptr && have) row_valid = p.valid[row] != 0;
     if (!mbar_wait(&full[s], (it / p.stages) & 1, p.status, kDevTimeoutEpilogue)) break;
     if (have) {
-      const float4* xs = reinterpret_cast<const float4*>(smem + s * stage_bytes) + static_cast<long long>(wr) * nv;
+      const uint8_t* xrow = smem + s * stage_bytes + static_cast<long long>(wr) * D * XS;
       const uint2* ds = reinterpret_cast<const uint2*>(smem + s * stage_bytes + x_bytes) + static_cast<long long>(wr) * nv;
       const bool keep = !(p.flags & TF_LN_MASK_DELTA) || row_valid;
       const bool zero_x = (p.flags & TF_LN_MASK_X) && !row_valid;
@@ -237,13 +285,20 @@ __global__ void __launch_bounds__(lns_threads(TEAMS), 1) ln_stream_kernel(const 
       for (int i = 0; i < NV; ++i) {
         const int c = lane + 32 * i;
         if (c < nv) {
-          const float4 a = xs[c];
-          v[i][0] = a.x; v[i][1] = a.y; v[i][2] = a.z; v[i][3] = a.w;
+          if constexpr (XT == kLnF32) {
+            const float4 a = reinterpret_cast<const float4*>(xrow)[c];
+            v[i][0] = a.x; v[i][1] = a.y; v[i][2] = a.z; v[i][3] = a.w;
+          } else {
+            widen4<DT>(reinterpret_cast<const uint2*>(xrow)[c], v[i]);
+          }
           if (has_delta && keep) {
-            const uint2 dq = ds[c];
-            const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&dq.x));
-            const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&dq.y));
-            v[i][0] += f0.x; v[i][1] += f0.y; v[i][2] += f1.x; v[i][3] += f1.y;
+            float d[4];
+            widen4<DT>(ds[c], d);
+            v[i][0] += d[0]; v[i][1] += d[1]; v[i][2] += d[2]; v[i][3] += d[3];
+            if constexpr (XT != kLnF32) {
+#pragma unroll
+              for (int j = 0; j < 4; ++j) v[i][j] = round16<DT>(v[i][j]);
+            }
           }
           if (zero_x) v[i][0] = v[i][1] = v[i][2] = v[i][3] = 0.f;
           sum += (v[i][0] + v[i][1]) + (v[i][2] + v[i][3]);
@@ -273,8 +328,15 @@ __global__ void __launch_bounds__(lns_threads(TEAMS), 1) ln_stream_kernel(const 
       for (int i = 0; i < NV; ++i) {
         const int c = lane + 32 * i;
         if (c < nv) {
-          if (p.flags & TF_LN_WRITE_X)
-            __stcs(reinterpret_cast<float4*>(p.x_out + row * D) + c, make_float4(v[i][0], v[i][1], v[i][2], v[i][3]));
+          if (p.flags & TF_LN_WRITE_X) {
+            if constexpr (XT == kLnF32) {
+              __stcs(reinterpret_cast<float4*>(static_cast<float*>(p.x_out) + row * D) + c,
+                     make_float4(v[i][0], v[i][1], v[i][2], v[i][3]));
+            } else {
+              __stcs(reinterpret_cast<uint2*>(static_cast<uint16_t*>(p.x_out) + row * D) + c,
+                     make_uint2(pack2<DT>(v[i][0], v[i][1]), pack2<DT>(v[i][2], v[i][3])));
+            }
+          }
           const float4 wv = reinterpret_cast<const float4*>(w_s)[c];
           const float4 bv = reinterpret_cast<const float4*>(b_s)[c];
           float y0 = (v[i][0] - mean) * rstd * wv.x + bv.x;
@@ -285,8 +347,8 @@ __global__ void __launch_bounds__(lns_threads(TEAMS), 1) ln_stream_kernel(const 
           if (p.flags & TF_LN_OUT_F32) {
             __stcs(reinterpret_cast<float4*>(static_cast<float*>(p.normed) + row * D) + c, make_float4(y0, y1, y2, y3));
           } else {
-            __stcs(reinterpret_cast<uint2*>(static_cast<__half*>(p.normed) + row * D) + c,
-                   make_uint2(pack_half2(y0, y1), pack_half2(y2, y3)));
+            __stcs(reinterpret_cast<uint2*>(static_cast<uint16_t*>(p.normed) + row * D) + c,
+                   make_uint2(pack2<DT>(y0, y1), pack2<DT>(y2, y3)));
           }
         }
       }
@@ -297,25 +359,15 @@ __global__ void __launch_bounds__(lns_threads(TEAMS), 1) ln_stream_kernel(const 
   }
 }
 
-int ln_residual(const float* x, const void* delta, const float* w, const float* b, float eps,
-                const uint8_t* valid, long long M, int D, int flags, float* x_out, void* normed,
-                cudaStream_t stream) {
-  if (M <= 0) return TF_OK;  // nothing to do
-  if (D <= 0 || D % 8 != 0 || D > 4096)
-    return set_error(TF_ERR_SHAPE, "ln_residual: D=%d must be a positive multiple of 8, <= 4096", D);
-  if (!aligned16(x) || !aligned16(delta) || !aligned16(w) || !aligned16(b) || !aligned16(x_out) ||
-      !aligned16(normed))
-    return set_error(TF_ERR_ALIGN, "ln_residual: pointers must be 16-byte aligned");
-  if (x == nullptr || w == nullptr || b == nullptr || normed == nullptr)
-    return set_error(TF_ERR_SHAPE, "ln_residual: x, w, b and normed are required");
-  if ((flags & TF_LN_WRITE_X) && x_out == nullptr) return set_error(TF_ERR_SHAPE, "ln_residual: WRITE_X without x_out");
-  if ((flags & (TF_LN_MASK_DELTA | TF_LN_MASK_X | TF_LN_MASK_OUT)) && valid == nullptr)
-    return set_error(TF_ERR_SHAPE, "ln_residual: mask flag without a valid-token mask");
-  if (!(flags & (TF_LN_MASK_DELTA | TF_LN_MASK_X | TF_LN_MASK_OUT))) valid = nullptr;
+template <int XT>
+static int ln_launch(const void* x, const void* delta, const float* w, const float* b, float eps,
+                     const uint8_t* valid, long long M, int D, int flags, void* x_out, void* normed,
+                     cudaStream_t stream) {
+  constexpr int XS = XT == kLnF32 ? 4 : 2;
   if (D <= 2048) {
     LnsParams lp;
     lp.x = x;
-    lp.delta = static_cast<const __half*>(delta);
+    lp.delta = static_cast<const uint16_t*>(delta);
     lp.w = w;
     lp.b = b;
     lp.valid = valid;
@@ -327,7 +379,7 @@ int ln_residual(const float* x, const void* delta, const float* w, const float* 
     lp.eps = eps;
     lp.status = device_status_ptr();
     if (lp.status == nullptr) return last_error_code();
-    const int stage_bytes = kLnsRows * D * (delta != nullptr ? 6 : 4);
+    const int stage_bytes = kLnsRows * D * (XS + (delta != nullptr ? 2 : 0));
     // teams and stages (a multiple of the team count, see the kernel's
     // stage-ownership note), best measured at the c3/c4 shapes: three teams
     // with six stages (D <= 1024 without delta), two with four (D = 1024 with
@@ -348,13 +400,15 @@ int ln_residual(const float* x, const void* delta, const float* w, const float* 
   {                                                                                                 \
     static bool attr_done[64] = {};                                                                 \
     if (!attr_done[dev & 63]) {                                                                     \
-      cudaError_t ea = cudaFuncSetAttribute(ln_stream_kernel<N, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+      cudaError_t ea = cudaFuncSetAttribute(ln_stream_kernel<N, T, XT>,                             \
+                                            cudaFuncAttributeMaxDynamicSharedMemorySize,            \
                                             kLnsSmemBudget + 8 * 2048 + 2 * kLnsMaxStages * 8 + 128); \
       if (ea != cudaSuccess)                                                                        \
         return set_error(TF_ERR_LAUNCH, "cudaFuncSetAttribute(ln): %s", cudaGetErrorString(ea));    \
       attr_done[dev & 63] = true;                                                                   \
     }                                                                                               \
-    launch_k(ln_stream_kernel<N, T>, dim3(static_cast<unsigned>(grid)), dim3(lns_threads(T)), smem, stream, lp); \
+    launch_k(ln_stream_kernel<N, T, XT>, dim3(static_cast<unsigned>(grid)), dim3(lns_threads(T)), smem, stream, \
+             lp);                                                                                   \
   }                                                                                                 \
   break;
     const int nvc = nv <= 2 ? 2 : nv <= 4 ? 4 : nv <= 8 ? 8 : 16;
@@ -376,16 +430,16 @@ int ln_residual(const float* x, const void* delta, const float* w, const float* 
   // grid-stride over rows with the device filled exactly (resident blocks
   // per SM from the occupancy of this instantiation)
   const int nch = (D / 8 + 31) / 32;
-  const __half* dh = static_cast<const __half*>(delta);
+  const uint16_t* dh = static_cast<const uint16_t*>(delta);
   const long long need = (M + kLnRowsPerBlock - 1) / kLnRowsPerBlock;
 #define TFB_LN_CASE(N)                                                                                        \
   {                                                                                                           \
     int per_sm = 1;                                                                                           \
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, ln_residual_kernel<N>, 256, 0);                    \
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, ln_residual_kernel<N, XT>, 256, 0);                \
     long long blocks = static_cast<long long>(device_sm_count()) * (per_sm > 0 ? per_sm : 1);                 \
     if (blocks > need) blocks = need;                                                                         \
-    launch_k(ln_residual_kernel<N>, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, stream, x, dh, w, b, eps, \
-             valid, M, D, flags, x_out, normed);                                                             \
+    launch_k(ln_residual_kernel<N, XT>, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, stream, x, dh, w, b, \
+             eps, valid, M, D, flags, x_out, normed);                                                        \
   }                                                                                                           \
   break;
   switch (nch <= 1 ? 1 : nch <= 2 ? 2 : nch <= 4 ? 4 : nch <= 8 ? 8 : 16) {
@@ -399,6 +453,30 @@ int ln_residual(const float* x, const void* delta, const float* w, const float* 
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(TF_ERR_LAUNCH, "ln_residual launch: %s", cudaGetErrorString(e));
   return TF_OK;
+}
+
+int ln_residual(const void* x, const void* delta, const float* w, const float* b, float eps,
+                const uint8_t* valid, long long M, int D, int flags, void* x_out, void* normed,
+                cudaStream_t stream) {
+  if (M <= 0) return TF_OK;  // nothing to do
+  if (D <= 0 || D % 8 != 0 || D > 4096)
+    return set_error(TF_ERR_SHAPE, "ln_residual: D=%d must be a positive multiple of 8, <= 4096", D);
+  if ((flags & TF_LN_X_F16) && (flags & TF_LN_X_BF16))
+    return set_error(TF_ERR_SHAPE, "ln_residual: TF_LN_X_F16 and TF_LN_X_BF16 together");
+  if (!aligned16(x) || !aligned16(delta) || !aligned16(w) || !aligned16(b) || !aligned16(x_out) ||
+      !aligned16(normed))
+    return set_error(TF_ERR_ALIGN, "ln_residual: pointers must be 16-byte aligned");
+  if (x == nullptr || w == nullptr || b == nullptr || normed == nullptr)
+    return set_error(TF_ERR_SHAPE, "ln_residual: x, w, b and normed are required");
+  if ((flags & TF_LN_WRITE_X) && x_out == nullptr) return set_error(TF_ERR_SHAPE, "ln_residual: WRITE_X without x_out");
+  if ((flags & (TF_LN_MASK_DELTA | TF_LN_MASK_X | TF_LN_MASK_OUT)) && valid == nullptr)
+    return set_error(TF_ERR_SHAPE, "ln_residual: mask flag without a valid-token mask");
+  if (!(flags & (TF_LN_MASK_DELTA | TF_LN_MASK_X | TF_LN_MASK_OUT))) valid = nullptr;
+  if (flags & TF_LN_X_BF16)
+    return ln_launch<kLnBF16>(x, delta, w, b, eps, valid, M, D, flags, x_out, normed, stream);
+  if (flags & TF_LN_X_F16)
+    return ln_launch<kLnF16>(x, delta, w, b, eps, valid, M, D, flags, x_out, normed, stream);
+  return ln_launch<kLnF32>(x, delta, w, b, eps, valid, M, D, flags, x_out, normed, stream);
 }
 
 }  // namespace tfb

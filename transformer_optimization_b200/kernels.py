@@ -29,22 +29,32 @@ def _need_cuda(name: str, *ts: Optional[torch.Tensor]) -> None:
             raise RuntimeError(f"{name}: every operand must be a CUDA tensor (no CPU path)")
 
 
+HALF_TYPES = (torch.float16, torch.bfloat16)
+
+
 def ln_residual(x: torch.Tensor, delta: Optional[torch.Tensor], weight: torch.Tensor, bias: torch.Tensor,
                 eps: float, valid: Optional[torch.Tensor] = None, *, mask_delta: bool = False,
                 mask_x: bool = False, mask_out: bool = False, write_x: bool = False,
-                x_out: Optional[torch.Tensor] = None, out_dtype: torch.dtype = torch.float16,
+                x_out: Optional[torch.Tensor] = None, out_dtype: Optional[torch.dtype] = None,
                 normed: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, torch.Tensor]:
-    """One residual site (tf_ln_residual). x: fp32 [..., D] contiguous; delta:
-    fp16 of the same shape or None; valid: bool/uint8 [rows] or None.
+    """One residual site (tf_ln_residual). x: fp32 [..., D] contiguous with
+    delta fp16 of the same shape or None (the fp32 model), or x fp16/bf16 with
+    delta of x's type (a half-precision model: x + delta is rounded to that
+    type); weight and bias fp32; valid: bool/uint8 [rows] or None. normed is
+    fp16 (fp32 x) or x's type (half x) unless out_dtype is fp32.
     Returns (x_new, normed); x_new is x_out (may be x itself: the kernel reads
     each row fully before writing it) when write_x, else x."""
     _need_cuda("ln_residual", x, delta, weight, bias, valid, x_out, normed)
-    if x.dtype != torch.float32 or not x.is_contiguous():
-        raise ValueError("ln_residual: x must be contiguous fp32")
+    if x.dtype not in (torch.float32,) + HALF_TYPES or not x.is_contiguous():
+        raise ValueError("ln_residual: x must be contiguous fp32, fp16 or bf16")
+    half = x.dtype in HALF_TYPES
     d = x.shape[-1]
     m = x.numel() // d
-    if delta is not None and (delta.dtype != torch.float16 or not delta.is_contiguous() or delta.numel() != x.numel()):
-        raise ValueError("ln_residual: delta must be contiguous fp16 shaped like x")
+    delta_dtype = x.dtype if half else torch.float16
+    if delta is not None and (delta.dtype != delta_dtype or not delta.is_contiguous() or delta.numel() != x.numel()):
+        raise ValueError(f"ln_residual: delta must be contiguous {delta_dtype} shaped like x")
+    if weight.dtype != torch.float32 or bias.dtype != torch.float32:
+        raise ValueError("ln_residual: weight and bias must be fp32")
     flags = 0
     if mask_delta:
         flags |= _abi.TF_LN_MASK_DELTA
@@ -62,10 +72,16 @@ def ln_residual(x: torch.Tensor, delta: Optional[torch.Tensor], weight: torch.Te
         flags |= _abi.TF_LN_WRITE_X
         if x_out is None:
             x_out = torch.empty_like(x)
+    if x.dtype == torch.float16:
+        flags |= _abi.TF_LN_X_F16
+    elif x.dtype == torch.bfloat16:
+        flags |= _abi.TF_LN_X_BF16
+    if out_dtype is None:
+        out_dtype = x.dtype if half else torch.float16
     if out_dtype == torch.float32:
         flags |= _abi.TF_LN_OUT_F32
-    elif out_dtype != torch.float16:
-        raise ValueError("ln_residual: out_dtype must be fp16 or fp32")
+    elif out_dtype != delta_dtype:
+        raise ValueError(f"ln_residual: out_dtype must be {delta_dtype} or fp32")
     if normed is None:
         normed = torch.empty(x.shape, dtype=out_dtype, device=x.device)
     _abi.call("tf_ln_residual", _ptr(x), _ptr(delta), _ptr(weight), _ptr(bias), float(eps),
@@ -75,8 +91,10 @@ def ln_residual(x: torch.Tensor, delta: Optional[torch.Tensor], weight: torch.Te
 
 def _gemm_operands(name, a, w, b, w_split):
     _need_cuda(name, a, w, b)
-    if a.dtype != torch.float16 or w.dtype != torch.float16:
-        raise ValueError(f"{name}: a and w must be fp16")
+    if a.dtype not in HALF_TYPES or w.dtype != a.dtype:
+        raise ValueError(f"{name}: a and w must both be fp16 or both bf16")
+    if w_split and a.dtype != torch.float16:
+        raise ValueError(f"{name}: split weights are fp16")
     if b.dtype != torch.float32 or not b.is_contiguous():
         raise ValueError(f"{name}: bias must be contiguous fp32")
     k = a.shape[-1]
@@ -117,28 +135,35 @@ def _splitk_ws(workspace: Optional[torch.Tensor], m: int, n: int, k: int, splits
 
 def linear(a: torch.Tensor, w: torch.Tensor, b: torch.Tensor, *, gelu: bool = False,
            out: Optional[torch.Tensor] = None, tile_n: int = 0, w_split: bool = False,
-           pair: int = 0, splits: Optional[int] = None, workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """fp16 GEMM on tcgen05 (tf_gemm): out = fp16([gelu](a @ w.T + b)), a
-    [..., K] fp16 with unit inner stride, w [N, K] fp16 (or split_weight's
-    [N, 2K] with w_split), b [N] fp32. splits (0 = automatic) selects the
-    split-K form (tf_gemm_splitk) with `workspace` (allocated if None)."""
+           pair: int = 0, splits: Optional[int] = None, workspace: Optional[torch.Tensor] = None,
+           round_gelu_input: bool = False) -> torch.Tensor:
+    """16-bit GEMM on tcgen05 (tf_gemm): out = T([gelu](a @ w.T + b)) with T
+    = a's type, a [..., K] fp16 or bf16 with unit inner stride, w [N, K] of
+    the same type (or split_weight's fp16 [N, 2K] with w_split), b [N] fp32.
+    round_gelu_input: GELU of T(a @ w.T + b), as F.gelu applied to a stored
+    Linear output of a half-precision model. splits (0 = automatic) selects
+    the split-K form (tf_gemm_splitk) with `workspace` (allocated if None)."""
     a2, n, k = _gemm_operands("linear", a, w, b, w_split)
     _need_cuda("linear", out)
     m = a2.shape[0]
     if out is None:
-        out = torch.empty(*a.shape[:-1], n, dtype=torch.float16, device=a.device)
+        out = torch.empty(*a.shape[:-1], n, dtype=a.dtype, device=a.device)
     o2 = out.view(-1, n) if out.is_contiguous() else out
-    if o2.stride(-1) != 1 or o2.dtype != torch.float16:
-        raise ValueError("linear: out must be fp16 with a unit inner stride")
+    if o2.stride(-1) != 1 or o2.dtype != a.dtype:
+        raise ValueError("linear: out must have a's type and a unit inner stride")
+    epi = _abi.TF_EPI_BIAS
+    if gelu:
+        epi = _abi.TF_EPI_BIAS_GELU_ROUNDED if round_gelu_input else _abi.TF_EPI_BIAS_GELU
+    if a.dtype == torch.bfloat16:
+        epi |= _abi.TF_EPI_BF16
     if splits is not None:
         if w_split:
             raise ValueError("linear: split-K does not take split weights")
         ws = _splitk_ws(workspace, m, n, k, splits, a.device)
         _abi.call("tf_gemm_splitk", _ptr(a2), a2.stride(0), _ptr(w), w.stride(0), _ptr(b), _ptr(o2), o2.stride(0),
-                  m, n, k, _abi.TF_EPI_BIAS_GELU if gelu else _abi.TF_EPI_BIAS, int(splits), _ptr(ws),
-                  ws.numel() * ws.element_size(), _stream())
+                  m, n, k, epi, int(splits), _ptr(ws), ws.numel() * ws.element_size(), _stream())
         return out
-    epi = (_abi.TF_EPI_BIAS_GELU if gelu else _abi.TF_EPI_BIAS) | (_abi.TF_EPI_W_SPLIT if w_split else 0)
+    epi |= _abi.TF_EPI_W_SPLIT if w_split else 0
     if tile_n or pair:
         _abi.call("tf_gemm_tiled", _ptr(a2), a2.stride(0), _ptr(w), w.stride(0), _ptr(b), _ptr(o2), o2.stride(0),
                   m, n, k, epi, tile_n, pair, _stream())
@@ -153,17 +178,19 @@ def linear_residual(a: torch.Tensor, w: torch.Tensor, b: torch.Tensor, x_in: tor
                     mask_delta: bool = False, mask_x: bool = False, w_split: bool = False, tile_n: int = 0,
                     pair: int = 0, splits: Optional[int] = None,
                     workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """GEMM closing a residual connection in fp32 (tf_gemm_residual):
-    x_out = mask_x(x_in + mask_delta(a @ w.T + b)). x_in/x_out fp32 [..., N]
-    contiguous (x_out may be x_in); valid bool/uint8 [rows] for the masks.
+    """GEMM closing a residual connection (tf_gemm_residual):
+    x_out = mask_x(x_in + mask_delta(a @ w.T + b)). x_in/x_out [..., N]
+    contiguous (x_out may be x_in), fp32, or a's type for a half-precision
+    model (then both the Linear's output and the sum are rounded to it, as the
+    eager model stores them); valid bool/uint8 [rows] for the masks.
     splits (0 = automatic) selects tf_gemm_residual_splitk."""
     a2, n, k = _gemm_operands("linear_residual", a, w, b, w_split)
     _need_cuda("linear_residual", x_in, x_out, valid)
-    if x_in.dtype != torch.float32 or not x_in.is_contiguous() or x_in.shape[-1] != n:
-        raise ValueError("linear_residual: x_in must be contiguous fp32 [..., N]")
+    if x_in.dtype not in (torch.float32, a.dtype) or not x_in.is_contiguous() or x_in.shape[-1] != n:
+        raise ValueError("linear_residual: x_in must be contiguous fp32 or a's type [..., N]")
     if x_out is None:
         x_out = torch.empty_like(x_in)
-    if x_out.shape != x_in.shape or x_out.dtype != torch.float32 or not x_out.is_contiguous():
+    if x_out.shape != x_in.shape or x_out.dtype != x_in.dtype or not x_out.is_contiguous():
         raise ValueError("linear_residual: x_out must match x_in")
     m = a2.shape[0]
     if x_in.numel() // n != m:
@@ -173,6 +200,8 @@ def linear_residual(a: torch.Tensor, w: torch.Tensor, b: torch.Tensor, x_in: tor
     mode = _abi.TF_RES_MASK_DELTA if mask_delta else (_abi.TF_RES_MASK_X if mask_x else _abi.TF_RES_NO_MASK)
     if mode and (valid is None or valid.numel() != m or valid.dtype not in (torch.bool, torch.uint8)):
         raise ValueError("linear_residual: masking needs a bool/uint8 mask with one entry per row")
+    opts = (_abi.TF_RES_X16 if x_in.dtype != torch.float32 else 0) | (
+        _abi.TF_RES_BF16 if a.dtype == torch.bfloat16 else 0)
     if valid is not None and not valid.is_contiguous():
         valid = valid.contiguous()
     if splits is not None:
@@ -180,29 +209,35 @@ def linear_residual(a: torch.Tensor, w: torch.Tensor, b: torch.Tensor, x_in: tor
             raise ValueError("linear_residual: split-K does not take split weights")
         ws = _splitk_ws(workspace, m, n, k, splits, a.device)
         _abi.call("tf_gemm_residual_splitk", _ptr(a2), a2.stride(0), _ptr(w), w.stride(0), _ptr(b), _ptr(x_in),
-                  _ptr(x_out), n, _ptr(valid) if mode else None, mode, m, n, k, int(splits), _ptr(ws),
+                  _ptr(x_out), n, _ptr(valid) if mode else None, mode | opts, m, n, k, int(splits), _ptr(ws),
                   ws.numel() * ws.element_size(), _stream())
         return x_out
     _abi.call("tf_gemm_residual", _ptr(a2), a2.stride(0), _ptr(w), w.stride(0), _ptr(b), _ptr(x_in), _ptr(x_out), n,
-              _ptr(valid) if mode else None, mode, m, n, k, 1 if w_split else 0, tile_n, pair, _stream())
+              _ptr(valid) if mode else None, mode | opts, m, n, k, 1 if w_split else 0, tile_n, pair, _stream())
     return x_out
 
 
 def flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, heads: int, scale: float, *,
                     causal: bool = False, key_valid: Optional[torch.Tensor] = None, q_pos0: int = 0,
-                    k_pos0: int = 0, out: Optional[torch.Tensor] = None, out_dtype: torch.dtype = torch.float16,
+                    k_pos0: int = 0, out: Optional[torch.Tensor] = None, out_dtype: Optional[torch.dtype] = None,
                     lse: Optional[torch.Tensor] = None, want_lse: bool = False, exp_f16x2: bool = False,
                     fma_exp_pairs: int = 0):
     """Flash attention forward (tf_flash_fwd).
 
-    q: [B, Sq, H*hd] fp16 view with unit inner stride (may be a column slice
-    of a packed QKV buffer), k, v: [B, Sk, H*hd] likewise. Returns out
-    [B, Sq, H*hd] (fp16 or fp32) and, with want_lse or an lse buffer, the
-    natural-log sum-exp [B, H, Sq] fp32."""
+    q: [B, Sq, H*hd] fp16 or bf16 view with unit inner stride (may be a
+    column slice of a packed QKV buffer), k, v: [B, Sk, H*hd] likewise, of
+    q's type. Returns out [B, Sq, H*hd] (q's type unless out_dtype is fp32)
+    and, with want_lse or an lse buffer, the natural-log sum-exp [B, H, Sq]
+    fp32."""
     _need_cuda("flash_attention", q, k, v, key_valid, out, lse)
     for t in (q, k, v):
-        if t.dtype != torch.float16 or t.dim() != 3 or t.stride(-1) != 1:
-            raise ValueError("flash_attention: q, k, v must be fp16 [B, S, H*hd] with unit inner stride")
+        if t.dtype not in HALF_TYPES or t.dtype != q.dtype or t.dim() != 3 or t.stride(-1) != 1:
+            raise ValueError("flash_attention: q, k, v must be fp16 or bf16 [B, S, H*hd] (one type) with unit "
+                             "inner stride")
+    if out_dtype is None:
+        out_dtype = q.dtype
+    if out_dtype not in (q.dtype, torch.float32):
+        raise ValueError("flash_attention: out_dtype must be q's type or fp32")
     bsz, sq, dq = q.shape
     sk = k.shape[1]
     if k.shape != v.shape or k.shape[0] != bsz or k.shape[2] != dq or v.stride() != k.stride():
@@ -221,6 +256,8 @@ def flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, heads: in
             raise ValueError("flash_attention: key_valid must be bool [B, Sk]")
         key_valid = key_valid.contiguous()
     flags = (_abi.TF_ATTN_CAUSAL if causal else 0) | (_abi.TF_ATTN_OUT_F32 if out_dtype == torch.float32 else 0)
+    if q.dtype == torch.bfloat16:
+        flags |= _abi.TF_ATTN_BF16
     if exp_f16x2:
         flags |= _abi.TF_ATTN_EXP_F16X2
     flags |= (int(fma_exp_pairs) & 0xFF) << 8

@@ -6,14 +6,18 @@ reference's `BaselineTransformer` (torch_transformer_benchmark.py:135-248), so
 initialisation under a given seed draws the same weights.
 
 `UserOptimizedTransformer.forward(x, valid_token_mask=None)` keeps the
-reference's contract (torch_transformer_benchmark.py:3509-3611): fp32 [B,S,D]
-in, fp32 [B,S,D] out, the input is never mutated, the result never aliases
-internal buffers, and nothing new is registered as a parameter or buffer.
-Its arithmetic is the reference's fp32-model fast path
-(torch_transformer_benchmark.py:4130-4199): every GEMM and the attention run
-in fp16 with fp32 accumulation, residual stream and LayerNorm stay fp32. The
-kernels are this package's sm_100a CUDA code reached through the C ABI;
-there is no eager/CPU fallback.
+reference's contract (torch_transformer_benchmark.py:3509-3611): [B,S,D] in,
+[B,S,D] out of x's dtype, the input is never mutated, the result never
+aliases internal buffers, and nothing new is registered as a parameter or
+buffer. For the fp32 model its arithmetic is the reference's fp32-model fast
+path (torch_transformer_benchmark.py:4130-4199): every GEMM and the attention
+run in fp16 with fp32 accumulation, residual stream and LayerNorm stay fp32.
+fp16 and bf16 models (parameters and input of that type, T) run the same
+kernels on T operands and keep the eager model's roundings to T: every
+Linear output, the residual stream and the LayerNorm outputs are stored in T
+(torch_transformer_benchmark.py:162-248 run in T). The kernels are this
+package's sm_100a CUDA code reached through the C ABI; there is no eager/CPU
+fallback.
 """
 
 from __future__ import annotations
@@ -102,26 +106,32 @@ def copy_model_weights(baseline: nn.Module, optimized: nn.Module, strict: bool =
 
 
 class _LayerWeights:
-    """GEMM operands of one layer: fp16 weights (packed [3D, D] QKV, as the
-    reference packs them: torch_transformer_benchmark.py:440-504) and fp32
-    biases. With `split_ffn_out` the FFN-out weight is kept as [W_hi | W_lo]
+    """GEMM operands of one layer in the compute type `ct` (fp16 for the fp32
+    and fp16 models, bf16 for bf16 models): packed [3D, D] QKV as the
+    reference packs it (torch_transformer_benchmark.py:440-504), and fp32
+    biases and LayerNorm parameters (exact for every model type). With
+    `split_ffn_out` (fp32 model) the FFN-out weight is kept as [W_hi | W_lo]
     (kernels.split_weight) for a near-fp32 product."""
 
-    __slots__ = ("wqkv", "bqkv", "wo", "bo", "w1", "b1", "w2", "b2", "split_w2")
+    __slots__ = ("wqkv", "bqkv", "wo", "bo", "w1", "b1", "w2", "b2", "split_w2", "n1w", "n1b", "n2w", "n2b")
 
-    def __init__(self, blk: BaselineTransformerBlock, split_ffn_out: bool) -> None:
+    def __init__(self, blk: BaselineTransformerBlock, split_ffn_out: bool, ct: torch.dtype = torch.float16) -> None:
         at = blk.attention
         with torch.no_grad():
-            self.wqkv = torch.cat([at.q_proj.weight, at.k_proj.weight, at.v_proj.weight], 0).half().contiguous()
+            self.wqkv = torch.cat([at.q_proj.weight, at.k_proj.weight, at.v_proj.weight], 0).to(ct).contiguous()
             self.bqkv = torch.cat([at.q_proj.bias, at.k_proj.bias, at.v_proj.bias], 0).float().contiguous()
-            self.wo = at.out_proj.weight.half().contiguous()
+            self.wo = at.out_proj.weight.to(ct).contiguous()
             self.bo = at.out_proj.bias.float().contiguous()
-            self.w1 = blk.ffn_in.weight.half().contiguous()
+            self.w1 = blk.ffn_in.weight.to(ct).contiguous()
             self.b1 = blk.ffn_in.bias.float().contiguous()
             self.split_w2 = split_ffn_out
             self.w2 = (kernels.split_weight(blk.ffn_out.weight) if split_ffn_out
-                       else blk.ffn_out.weight.half().contiguous())
+                       else blk.ffn_out.weight.to(ct).contiguous())
             self.b2 = blk.ffn_out.bias.float().contiguous()
+            self.n1w = blk.norm1.weight.float().contiguous()
+            self.n1b = blk.norm1.bias.float().contiguous()
+            self.n2w = blk.norm2.weight.float().contiguous()
+            self.n2b = blk.norm2.bias.float().contiguous()
 
 
 def _splitk(m: int, n: int, k: int, sms: int) -> Optional[int]:
@@ -164,6 +174,7 @@ class UserOptimizedTransformer(BaselineTransformer):
         # plain attributes only: no parameters or buffers are added
         self._weights_key: Optional[Tuple] = None
         self._weights: Optional[list] = None
+        self._final_ln: Optional[Tuple[torch.Tensor, torch.Tensor]] = None  # fp32 final LayerNorm w, b
         self._graph_cache: Dict[Tuple, _GraphCacheEntry] = {}
         self._graph_unsupported: set = set()
         self._graph_pool = None
@@ -175,19 +186,28 @@ class UserOptimizedTransformer(BaselineTransformer):
         # where fp16 weight rounding accumulates over many residual adds).
         self.precise_ffn_out: Optional[bool] = None
 
+    def _model_dtype(self) -> torch.dtype:
+        return self.final_norm.weight.dtype
+
     def _split_ffn_out(self) -> bool:
+        if self._model_dtype() != torch.float32:
+            return False  # a half-precision model's weights are already in its own type
         if self.precise_ffn_out is not None:
             return bool(self.precise_ffn_out)
         return self.config.num_layers >= 16
 
     # ------------------------------------------------------------------ caches
     def _layer_weights(self) -> list:
-        """fp16 weight caches, rebuilt whenever a source parameter's storage,
-        dtype or device changes (torch_transformer_benchmark.py:452-466)."""
+        """Compute-type weight caches, rebuilt whenever a source parameter's
+        storage, dtype or device changes (torch_transformer_benchmark.py:
+        452-466)."""
         split = self._split_ffn_out()
         key = tuple((p.data_ptr(), p.dtype, p.device, p._version) for p in self.parameters()) + (split,)
         if self._weights is None or key != self._weights_key:
-            self._weights = [_LayerWeights(blk, split) for blk in self.layers]
+            ct = torch.bfloat16 if self._model_dtype() == torch.bfloat16 else torch.float16
+            fn = self.final_norm
+            self._weights = [_LayerWeights(blk, split, ct) for blk in self.layers]
+            self._final_ln = (fn.weight.float().contiguous(), fn.bias.float().contiguous())
             self._weights_key = key
             self._graph_cache.clear()
         return self._weights
@@ -213,9 +233,12 @@ class UserOptimizedTransformer(BaselineTransformer):
         """The per-layer schedule of torch_transformer_benchmark.py:4003-4326
         (fp16-GEMM branch 4130-4199). The residual adds of the reference's
         LayerNorm sites happen in the epilogues of out_proj and ffn_out
-        (fp32, same masking points: mask_delta after attention, mask_x after
-        the FFN); the LayerNorm kernels then only normalise. No host sync, so
-        it is safe to capture."""
+        (same masking points: mask_delta after attention, mask_x after the
+        FFN); the LayerNorm kernels then only normalise. The residual stream is
+        fp32 for the fp32 model and the model's type T for fp16/bf16 models
+        (whose epilogues round the Linear output and the sum to T, and whose
+        GELU reads the T-rounded Linear output). No host sync, so it is safe
+        to capture."""
         cfg = self.config
         b, s, d = x.shape
         h = cfg.num_heads
@@ -224,12 +247,14 @@ class UserOptimizedTransformer(BaselineTransformer):
         vflat = valid.reshape(-1) if mask_active else None
         kvalid = valid if mask_active else None
         dev = x.device
+        half = x.dtype != torch.float32
+        ct = wts[0].wqkv.dtype  # compute (operand) type
 
-        x_res = torch.empty(b, s, d, dtype=torch.float32, device=dev)
-        normed = torch.empty(b, s, d, dtype=torch.float16, device=dev)
-        qkv = torch.empty(b, s, 3 * d, dtype=torch.float16, device=dev)
-        ctx = torch.empty(b, s, d, dtype=torch.float16, device=dev)
-        hidden = torch.empty(b, s, cfg.ffn_dim, dtype=torch.float16, device=dev)
+        x_res = torch.empty(b, s, d, dtype=x.dtype, device=dev)
+        normed = torch.empty(b, s, d, dtype=ct, device=dev)
+        qkv = torch.empty(b, s, 3 * d, dtype=ct, device=dev)
+        ctx = torch.empty(b, s, d, dtype=ct, device=dev)
+        hidden = torch.empty(b, s, cfg.ffn_dim, dtype=ct, device=dev)
 
         # split-K (fp32 partials in a workspace) for the projections of
         # few-row inputs, where 128-row tiles would leave most SMs idle
@@ -248,19 +273,20 @@ class UserOptimizedTransformer(BaselineTransformer):
         cur = x  # residual stream; the caller's x is read, never written
         for li, blk in enumerate(self.layers):
             w = wts[li]
-            kernels.ln_residual(cur, None, blk.norm1.weight, blk.norm1.bias, blk.norm1.eps, normed=normed)
+            kernels.ln_residual(cur, None, w.n1w, w.n1b, blk.norm1.eps, normed=normed)
             kernels.linear(normed, w.wqkv, w.bqkv, out=qkv, splits=sk_qkv, workspace=ws)
             kernels.flash_attention(qkv[..., :d], qkv[..., d:2 * d], qkv[..., 2 * d:], h, scale,
                                     causal=cfg.causal, key_valid=kvalid, out=ctx)
             cur = kernels.linear_residual(ctx, w.wo, w.bo, cur, x_res, vflat, mask_delta=mask_active,
                                           splits=sk_o, workspace=ws)
-            kernels.ln_residual(cur, None, blk.norm2.weight, blk.norm2.bias, blk.norm2.eps, normed=normed)
-            kernels.linear(normed, w.w1, w.b1, gelu=True, out=hidden, splits=sk_1, workspace=ws)
+            kernels.ln_residual(cur, None, w.n2w, w.n2b, blk.norm2.eps, normed=normed)
+            kernels.linear(normed, w.w1, w.b1, gelu=True, out=hidden, splits=sk_1, workspace=ws,
+                           round_gelu_input=half)
             kernels.linear_residual(hidden, w.w2, w.b2, cur, x_res, vflat, mask_x=mask_active,
                                     w_split=w.split_w2, splits=sk_2, workspace=ws)
-        fn = self.final_norm
-        _, out = kernels.ln_residual(cur, None, fn.weight, fn.bias, fn.eps, vflat, mask_out=mask_active,
-                                     out_dtype=torch.float32)
+        fw, fb = self._final_ln
+        _, out = kernels.ln_residual(cur, None, fw, fb, self.final_norm.eps, vflat, mask_out=mask_active,
+                                     out_dtype=x.dtype)
         return out
 
     # ------------------------------------------------------------------ graphs
@@ -295,8 +321,11 @@ class UserOptimizedTransformer(BaselineTransformer):
         cfg = self.config
         if not x.is_cuda:
             raise RuntimeError("UserOptimizedTransformer needs a CUDA (B200) tensor; there is no CPU path")
-        if x.dtype != torch.float32 or self.final_norm.weight.dtype != torch.float32:
-            raise NotImplementedError("only the fp32 model (fp16 tensor-core compute) is implemented")
+        if x.dtype not in (torch.float32, torch.float16, torch.bfloat16):
+            raise NotImplementedError(f"input dtype {x.dtype}: fp32, fp16 and bf16 models are implemented")
+        if self._model_dtype() != x.dtype:
+            raise ValueError(f"x is {x.dtype} but the model's parameters are {self._model_dtype()}: convert both "
+                             "to one dtype (model.to(dtype) and x.to(dtype))")
         if x.dim() != 3 or x.shape[-1] != cfg.d_model:
             raise ValueError(f"expected x of shape [B, S, {cfg.d_model}], got {tuple(x.shape)}")
         if not x.is_contiguous():
@@ -311,7 +340,7 @@ class UserOptimizedTransformer(BaselineTransformer):
 
         if not self.use_cuda_graphs or not self._graph_memory_safe(x):
             return self._forward_core(x, valid_token_mask, mask_active)
-        key = (tuple(x.shape), x.device, cfg.causal, mask_kind, self._split_ffn_out())
+        key = (tuple(x.shape), x.dtype, x.device, cfg.causal, mask_kind, self._split_ffn_out())
         if key in self._graph_unsupported:
             return self._forward_core(x, valid_token_mask, mask_active)
         self._layer_weights()  # may invalidate cached graphs
