@@ -60,15 +60,16 @@ def load_peaks():
     return dict(FALLBACK_PEAKS), "fallback"
 
 
-def algo_bytes_per_gemm(cfg):
+def algo_bytes_per_gemm(cfg, x_bytes=4):
     """Mean algorithmic HBM bytes of the four projections of one layer:
-    fp16 A and W read, fp16 C written (QKV, FFN in), or fp32 x read and
-    written around the product (the two residual projections)."""
+    16-bit A and W read, 16-bit C written (QKV, FFN in), or the residual x
+    (x_bytes per element: 4 for the fp32 model, 2 for fp16/bf16 models) read
+    and written around the product (the two residual projections)."""
     m, d, f = cfg.batch_size * cfg.seq_len, cfg.d_model, cfg.ffn_dim
     qkv = 2 * (m * d + 3 * d * d + 3 * m * d)
     ffn_in = 2 * (m * d + f * d + m * f)
-    out_proj = 2 * (m * d + d * d) + 8 * m * d
-    ffn_out = 2 * (m * f + d * f) + 8 * m * d
+    out_proj = 2 * (m * d + d * d) + 2 * x_bytes * m * d
+    ffn_out = 2 * (m * f + d * f) + 2 * x_bytes * m * d
     return (qkv + ffn_in + out_proj + ffn_out) / 4
 
 
@@ -129,11 +130,14 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------- helpers
-def build_model(cfg, device):
+MODEL_DTYPES = {"float32": torch.float32, "float16": torch.float16, "bfloat16": torch.bfloat16}
+
+
+def build_model(cfg, device, dtype=torch.float32):
     torch.manual_seed(0)
     with torch.device(device):
         model = UserOptimizedTransformer(cfg)
-    return model.eval()
+    return model.to(dtype).eval()
 
 
 def flush_l2(buf):
@@ -223,10 +227,10 @@ def kernel_profile(model, x):
         return 4.0 * bsz * sq * sk * dq  # dense count (run_bench.py convention)
 
     def ln_bytes(x, delta, w, b, eps, valid=None, **kw):
-        n = x.numel()
-        by = n * 4 + (n * 2 if delta is not None else 0)
-        by += n * 4 if kw.get("write_x") else 0
-        by += n * (4 if kw.get("out_dtype", torch.float16) == torch.float32 else 2)
+        n, xs = x.numel(), x.element_size()
+        by = n * xs + (n * 2 if delta is not None else 0)
+        by += n * xs if kw.get("write_x") else 0
+        by += n * (4 if kw.get("out_dtype") == torch.float32 else 2)
         return float(by)
 
     K.linear = wrap("gemm", orig[0], gemm_flops)
@@ -305,9 +309,9 @@ def run_reference(args, cfg, rank):
     print(json.dumps(line), flush=True)
 
 
-def measure_config(cfg, device, steps, warmup, flush_buf):
-    model = build_model(cfg, device)
-    x = torch.randn(cfg.batch_size, cfg.seq_len, cfg.d_model, device=device)
+def measure_config(cfg, device, steps, warmup, flush_buf, dtype=torch.float32):
+    model = build_model(cfg, device, dtype)
+    x = torch.randn(cfg.batch_size, cfg.seq_len, cfg.d_model, device=device).to(dtype)
     with torch.inference_mode():
         for _ in range(warmup):
             model(x)
@@ -326,8 +330,9 @@ def run_ours(args, cfg, rank, world, local_rank):
     peaks, peak_src = load_peaks()
     flush_buf = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
 
-    model = build_model(cfg, device)
-    x = torch.randn(cfg.batch_size, cfg.seq_len, cfg.d_model, device=device)
+    mdt = MODEL_DTYPES[args.model_dtype]
+    model = build_model(cfg, device, mdt)
+    x = torch.randn(cfg.batch_size, cfg.seq_len, cfg.d_model, device=device).to(mdt)
     tokens = cfg.batch_size * cfg.seq_len
     with torch.inference_mode():
         for _ in range(max(args.warmup, 3)):
@@ -355,7 +360,7 @@ def run_ours(args, cfg, rank, world, local_rank):
     value = world * tokens / (ms_per_step / 1000.0)
 
     # ---- end to end through the public module: pinned host in, host out ----
-    x_host = torch.randn(cfg.batch_size, cfg.seq_len, cfg.d_model).pin_memory()
+    x_host = torch.randn(cfg.batch_size, cfg.seq_len, cfg.d_model).to(mdt).pin_memory()
     y_host = torch.empty_like(x_host).pin_memory()
     with torch.inference_mode():
         e2e_pipelined(model, x_host, y_host, 2, device)  # warm-up (allocations, streams)
@@ -387,23 +392,25 @@ def run_ours(args, cfg, rank, world, local_rank):
     line = {
         "metric": f"forward tokens/s ({args.config})", "value": value, "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16" if mdt == torch.bfloat16 else "f16",
+        "data": "synthetic",
         "config": {"workload": args.config, **cfg_dict(cfg), "global_batch": cfg.batch_size * world,
                    "parallelism": f"dp{world}", "l2": "flushed between steps (256 MB write)",
-                   "weights": "default init, seed 0", "cuda_graph": True},
+                   "weights": "default init, seed 0", "cuda_graph": True, "model_dtype": args.model_dtype},
         "mfu": flops / (ms_per_step / 1e3) / (tensor_peak * 1e12),
         "latency_ms": ms_per_step, "latency_ms_median": statistics.median(ts),
-        "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": x_host.numel() * 4,
-                "d2h_bytes_per_step": y_host.numel() * 4, "ms_per_step": e_total / args.steps,
+        "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": x_host.numel() * x_host.element_size(),
+                "d2h_bytes_per_step": y_host.numel() * y_host.element_size(), "ms_per_step": e_total / args.steps,
                 "copies": "pinned H2D and D2H every step on two copy streams, overlapping the neighbouring "
                           "steps' forwards; one event pair from the first upload to the last download"},
         "gpu_launches": launches_per_step * args.steps,
         "roofline": {"bound": "tensor", "kernel": "gemm_f16_tcgen05", "achieved": gemm_tflops,
                      "peak": sustained, "unit": "TFLOP/s", "frac": gemm_tflops / sustained,
                      "peak_source": f"bf16_tflops_sustained ({peak_src}): the GEMMs are timed inside the step",
-                     "traffic": C3_GEMM_DRAM_BYTES_PER_LAUNCH if args.config == "c3" else None,
+                     "traffic": (C3_GEMM_DRAM_BYTES_PER_LAUNCH
+                                 if args.config == "c3" and mdt == torch.float32 else None),
                      "traffic_unit": "bytes per launch (ncu dram read+write)",
-                     "algorithmic_bytes_per_launch": algo_bytes_per_gemm(cfg),
+                     "algorithmic_bytes_per_launch": algo_bytes_per_gemm(cfg, x.element_size()),
                      "launches_per_step": n_g, "gemm_share_of_step": ms_g / ms_per_step},
         "kernels": {
             "flash_fwd_tcgen05": {"launches": n_f, "ms": ms_f, "tflops": flash_tflops,
@@ -424,7 +431,7 @@ def run_ours(args, cfg, rank, world, local_rank):
             if name == args.config:
                 ts_c = ts
             else:
-                ts_c = measure_config(c, device, max(3, args.steps // 4), 3, flush_buf)
+                ts_c = measure_config(c, device, max(3, args.steps // 4), 3, flush_buf, mdt)
             lat = statistics.median(ts_c)
             per[name] = {"latency_ms": lat, "tokens_per_s": c.batch_size * c.seq_len / (lat / 1e3),
                          "mfu": count_dense_flops(c) / (lat / 1e3) / (tensor_peak * 1e12)}
@@ -515,6 +522,8 @@ def main():
     ap.add_argument("--config", default="c3", choices=sorted(NAMED_CONFIGS))
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
     ap.add_argument("--no-extra", action="store_true", help="skip per_config and cpu_baseline")
+    ap.add_argument("--model-dtype", default="float32", choices=sorted(MODEL_DTYPES),
+                    help="parameter and input dtype of the model (the BASELINE configs are float32)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -538,6 +547,8 @@ def main():
                                 device_id=torch.device("cuda", local_rank))
     try:
         if world > 1 and cfg.batch_size == 1:
+            if args.model_dtype != "float32":
+                raise SystemExit("context parallelism runs the float32 model")
             run_cp(args, cfg, rank, world, local_rank)  # one sequence: context parallel
         else:
             run_ours(args, cfg, rank, world, local_rank)
