@@ -217,6 +217,26 @@ def padded_mask(cfg, padding_ratio: float, seed: int) -> torch.Tensor:
     return torch.arange(cfg.seq_len)[None, :] < lengths[:, None]
 
 
+def harness_case(cfg, device, dtype: torch.dtype, seed: int, padding_ratio: float,
+                 input_scale: float) -> Tuple[torch.Tensor, torch.Tensor]:
+    """generate_random_case (torch_transformer_benchmark.py:4359-4397), the
+    harness's per-trial input: x ~ N(0,1) * input_scale from a generator on
+    `device` seeded with `seed`; with padding_ratio > 0, per-row valid lengths
+    drawn from the same generator and x zeroed at the padded tokens; the mask
+    is all True otherwise (the harness always passes one)."""
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    x = torch.randn(cfg.batch_size, cfg.seq_len, cfg.d_model, generator=g, device=device, dtype=dtype)
+    x = x * input_scale
+    if padding_ratio <= 0:
+        return x, torch.ones(cfg.batch_size, cfg.seq_len, device=device, dtype=torch.bool)
+    min_valid = max(1, int(round(cfg.seq_len * (1.0 - padding_ratio))))
+    lengths = torch.randint(low=min_valid, high=cfg.seq_len + 1, size=(cfg.batch_size,), generator=g,
+                            device=device)
+    mask = torch.arange(cfg.seq_len, device=device)[None, :] < lengths[:, None]
+    return x.masked_fill(~mask[..., None], 0), mask
+
+
 # --------------------------------------------------------------------------
 # Accuracy gate (torch_transformer_benchmark.py:4534-4615)
 # --------------------------------------------------------------------------

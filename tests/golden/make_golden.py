@@ -140,6 +140,22 @@ def main(ref_root: str) -> None:
         print(name, tuple(y.shape), float(y.double().sum()))
     torch.save(half, HERE / "golden_half_cases.pt")
 
+    # the harness's random inputs (generate_random_case) on the CPU
+    cases = {}
+    for name, (b, s, d, h, f, l, seed, pad, scale) in {
+        "c1_seed1234": (2, 128, 256, 4, 1024, 2, 1234, 0.0, 1.0),
+        "c1_seed1236_pad": (2, 128, 256, 4, 1024, 2, 1236, 0.4, 1.0),
+        "c2_seed1235_pad_scaled": (1, 64, 512, 8, 2048, 6, 1235, 0.5, 3.0),
+    }.items():
+        cfg = ttb.TransformerConfig(b, s, d, h, f, l, False)
+        x, mask = ttb.generate_random_case(cfg, torch.device("cpu"), torch.float32, seed, pad, scale)
+        xd = x.double().flatten()
+        w = torch.arange(1, xd.numel() + 1, dtype=torch.float64) % 97
+        cases[name] = {"args": (b, s, d, h, f, l, seed, pad, scale), "x_head": x.flatten()[:64].clone(),
+                       "x_checksum": torch.stack([xd.sum(), (xd * xd).sum(), (xd * w).sum()]),
+                       "mask": mask.clone()}
+    torch.save({"torch_version": torch.__version__, "cases": cases}, HERE / "golden_harness_inputs.pt")
+
 
 if __name__ == "__main__":
     if len(sys.argv) != 2:

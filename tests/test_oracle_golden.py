@@ -84,6 +84,26 @@ def test_oracle_half_matches_reference(name):
         assert torch.allclose(y.float(), rec["y"].float(), rtol=4 * ulp, atol=4 * ulp)
 
 
+GOLDEN_INPUTS = torch.load(Path(__file__).parent / "golden" / "golden_harness_inputs.pt", weights_only=False)
+
+
+@pytest.mark.parametrize("name", sorted(GOLDEN_INPUTS["cases"]))
+def test_harness_case_matches_reference(name):
+    """oracle.harness_case draws the harness's per-trial input and mask
+    (generate_random_case, torch_transformer_benchmark.py:4359-4397): same x
+    (checksums and first elements) and mask on the CPU."""
+    rec = GOLDEN_INPUTS["cases"][name]
+    b, s, d, h, f, l, seed, pad, scale = rec["args"]
+    cfg = TransformerConfig(b, s, d, h, f, l, False)
+    x, mask = om.harness_case(cfg, torch.device("cpu"), torch.float32, seed, pad, scale)
+    assert torch.equal(mask, rec["mask"])
+    assert torch.equal(x.flatten()[:64], rec["x_head"])
+    xd = x.double().flatten()
+    w = torch.arange(1, xd.numel() + 1, dtype=torch.float64) % 97
+    assert torch.allclose(torch.stack([xd.sum(), (xd * xd).sum(), (xd * w).sum()]), rec["x_checksum"],
+                          rtol=1e-12, atol=1e-9)
+
+
 def test_compare_outputs_or_criterion():
     """compare_outputs uses (abs<=atol) OR (abs<=rtol*|ref|), not isclose."""
     ref = torch.tensor([1.0, 0.1, 0.0, float("nan")])
