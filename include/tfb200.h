@@ -72,15 +72,16 @@ extern "C" {
 
 /* tf_flash_fwd flags */
 #define TF_ATTN_CAUSAL 1  /* mask key position > query position */
-#define TF_ATTN_OUT_F32 2 /* out is fp32 (default fp16) */
+#define TF_ATTN_OUT_F32 2 /* out is fp32 (default: q's type) */
 #define TF_ATTN_EXP_F16X2 4 /* packed fp16 exp2 for the probabilities (default:
                                fp32 exp2, the faster of the two on B200; P is
-                               rounded to fp16 for the PV product either way) */
+                               rounded to fp16 for the PV product either way);
+                               fp16 operands only */
 #define TF_ATTN_BF16 8      /* q, k, v and out (unless TF_ATTN_OUT_F32) are bf16;
                                P is rounded to bf16 for the PV product */
 /* flags bits 8..15: how many of the 64 probability pairs per row and key
  * block are exponentiated on the FMA pipes instead of the exp unit
- * (0, 8, 16 or 24; with TF_ATTN_EXP_F16X2: 0 or 16) */
+ * (0, 8, 16 or 24; with TF_ATTN_EXP_F16X2: 0 or 16; fp16 operands only) */
 #define TF_ATTN_FMA_EXP_SHIFT 8
 
 /* ABI version, bumped on any signature change. */
