@@ -166,6 +166,24 @@ int tf_gemm_residual_splitk(const void* A, int64_t lda, const void* W, int64_t l
                             int64_t M, int64_t N, int64_t K, int splits, void* workspace, int64_t workspace_bytes,
                             void* stream);
 
+/* tf_gemm_residual_splitk whose reduce kernel also runs the LayerNorm of the
+ * result (one warp per row):
+ *   x_out  = as tf_gemm_residual_splitk
+ *   normed = mask_out(LayerNorm(x_out) * ln_w + ln_b)      ([M, N] contiguous)
+ * normed is fp16 (the operand type with TF_RES_X16; fp32 with TF_LN_OUT_F32);
+ * ln_flags: TF_LN_MASK_OUT (rows where valid is 0 become 0), TF_LN_OUT_F32.
+ * ln_w, ln_b fp32 [N]; N <= 4096. For few-row inputs, where every kernel is
+ * bound by its launch and memory latency, this saves one launch per residual
+ * site over tf_gemm_residual_splitk followed by tf_ln_residual. Replaces
+ * out_proj / ffn_out with the residual add and the LayerNorm of the
+ * reference's next _ln_site (torch_transformer_benchmark.py:4163-4169, 4194,
+ * 3940-4001) or its final LayerNorm (4316-4325). */
+int tf_gemm_residual_ln_splitk(const void* A, int64_t lda, const void* W, int64_t ldw, const float* bias,
+                               const void* x_in, void* x_out, int64_t ldx, const uint8_t* valid, int mask_mode,
+                               int64_t M, int64_t N, int64_t K, int splits, void* workspace,
+                               int64_t workspace_bytes, const float* ln_w, const float* ln_b, float eps,
+                               void* normed, int ln_flags, void* stream);
+
 /* tf_gemm_splitk without a workspace argument: the fp32 partial sums go to a
  * fixed 4 MiB device array inside this library, so the call allocates
  * nothing and needs no caller-provided memory. For callers that cannot

@@ -142,6 +142,34 @@ def test_linear_residual_half(K, dt, m, n, k, kw, mode):
         assert torch.equal(out.cpu()[~valid], x[~valid])
 
 
+@pytest.mark.parametrize("dt", TYPES, ids=_name)
+@pytest.mark.parametrize("mode", ["none", "mask_delta", "mask_x"])
+def test_linear_residual_ln_half(K, dt, mode):
+    """The split-K residual site with its LayerNorm fused into the reduce, in
+    a half-precision stream: x_out as the unfused call (bit-identical), normed
+    within one ulp of T of the fp32 LayerNorm of x_out."""
+    m, n, k = 64, 512, 2048
+    g = torch.Generator().manual_seed(n + len(mode))
+    a = torch.randn(m, k, generator=g).to(dt)
+    w = (torch.randn(n, k, generator=g) * k ** -0.5).to(dt)
+    b = torch.randn(n, generator=g) * 0.1
+    x = (torch.randn(m, n, generator=g) * 3).to(dt)
+    valid = torch.rand(m, generator=g) > 0.25
+    lw = torch.randn(n, generator=g) * 0.1 + 1
+    lb = torch.randn(n, generator=g) * 0.1
+    md, mx = mode == "mask_delta", mode == "mask_x"
+    dv = torch.device("cuda:0")
+    args = (a.to(dv), w.to(dv), b.to(dv), x.to(dv))
+    x_new, normed = K.linear_residual_ln(*args, None, valid.to(dv), lw.to(dv), lb.to(dv), 1e-5, mask_delta=md,
+                                         mask_x=mx, splits=0)
+    unfused = K.linear_residual(*args, None, valid.to(dv), mask_delta=md, mask_x=mx, splits=0)
+    torch.cuda.synchronize()
+    assert x_new.dtype == dt and normed.dtype == dt
+    assert torch.equal(x_new, unfused)
+    _, yr = om.ln_site_half(x_new.cpu(), None, lw, lb, 1e-5, valid, False, False, False, dt)
+    _assert_within(normed, yr, ULP[dt] * yr.abs() + 1e-6, "normed")
+
+
 @pytest.mark.parametrize("b,h,sq,sk,hd,causal,masked", [
     (2, 4, 256, 256, 64, False, False),
     (1, 2, 300, 300, 64, True, False),

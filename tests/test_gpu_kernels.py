@@ -187,6 +187,39 @@ def test_gemm_residual_splitk(K, mode, m, k, n):
     assert torch.allclose(out.cpu(), ref, atol=1e-4, rtol=1e-5)
 
 
+@pytest.mark.parametrize("mode", ["none", "mask_delta", "mask_x", "final"])
+@pytest.mark.parametrize("m,k,n", [(64, 2048, 512), (256, 1024, 256), (200, 512, 1024), (37, 256, 4096)])
+def test_gemm_residual_ln_splitk(K, mode, m, k, n):
+    """Split-K residual projection whose reduce kernel also runs the
+    LayerNorm of the result: x_out bit-identical to the unfused split-K call,
+    normed against the oracle's LayerNorm of it (1 fp16 ulp; fp32 output
+    2e-5), masked rows of the final form zero."""
+    a, w, bias = _gemm_inputs(m, k, n, 7 * m + k + n)
+    w16 = w.half()
+    g = torch.Generator().manual_seed(m + n)
+    x = torch.randn(m, n, generator=g)
+    valid = torch.rand(m, generator=g) > 0.2
+    lw = torch.randn(n, generator=g) * 0.1 + 1
+    lb = torch.randn(n, generator=g) * 0.1
+    md, mx, mo = mode == "mask_delta", mode in ("mask_x", "final"), mode == "final"
+    out_dtype = torch.float32 if mode == "final" else torch.float16
+    dv = torch.device("cuda")
+    ag, wg, bg, xg, vg = a.to(dv), w16.to(dv), bias.to(dv), x.to(dv), valid.to(dv)
+    x_new, normed = K.linear_residual_ln(ag, wg, bg, xg, None, vg, lw.to(dv), lb.to(dv), 1e-5, mask_delta=md,
+                                         mask_x=mx, mask_out=mo, out_dtype=out_dtype, splits=0)
+    unfused = K.linear_residual(ag, wg, bg, xg, None, vg, mask_delta=md, mask_x=mx, splits=0)
+    torch.cuda.synchronize()
+    assert torch.equal(x_new, unfused)
+    ref_x = om.linear_residual(a, w16, bias, x, valid, md, mx)
+    assert torch.allclose(x_new.cpu(), ref_x, atol=1e-4, rtol=1e-5)
+    _, yr = om.ln_site(x_new.cpu(), None, lw, lb, 1e-5, valid, False, False, mo)
+    if out_dtype == torch.float32:
+        assert torch.allclose(normed.cpu(), yr, atol=2e-5, rtol=1e-5)
+        assert torch.count_nonzero(normed.cpu()[~valid]) == 0
+    else:
+        assert torch.allclose(normed.float().cpu(), yr.half().float(), atol=2e-3, rtol=1e-3)
+
+
 def test_gemm_splitk_workspace_checks(K):
     from transformer_optimization_b200 import _abi
     a, w, bias = _gemm_inputs(64, 1024, 256, 1)

@@ -166,7 +166,7 @@ static inline int begin_call() {
 
 extern "C" {
 
-int tf_abi_version(void) { return 8; }
+int tf_abi_version(void) { return 9; }
 
 const char* tf_last_error(void) { return tfb::g_msg; }
 
@@ -383,6 +383,37 @@ int tf_gemm_residual_splitk(const void* A, int64_t lda, const void* W, int64_t l
   g.dtype = dtype;
   g.a_repeat = 1;
   return tfb::gemm_splitk_f16(g, splits, static_cast<float*>(workspace), workspace_bytes, as_stream(stream));
+}
+
+int tf_gemm_residual_ln_splitk(const void* A, int64_t lda, const void* W, int64_t ldw, const float* bias,
+                               const void* x_in, void* x_out, int64_t ldx, const uint8_t* valid, int mask_mode,
+                               int64_t M, int64_t N, int64_t K, int splits, void* workspace,
+                               int64_t workspace_bytes, const float* ln_w, const float* ln_b, float eps,
+                               void* normed, int ln_flags, void* stream) {
+  int rc = begin_call();
+  if (rc) return rc;
+  int epi = 0, mask = 0, dtype = 0;
+  if (!residual_mode(mask_mode, epi, mask, dtype))
+    return set_error(TF_ERR_SHAPE, "tf_gemm_residual_ln_splitk: mask_mode=%d", mask_mode);
+  tfb::GemmCall g = {};
+  g.A = A;
+  g.lda = lda;
+  g.W = W;
+  g.ldw = ldw;
+  g.bias = bias;
+  g.x_in = x_in;
+  g.x_out = x_out;
+  g.ldx = ldx;
+  g.valid = valid;
+  g.mask_mode = mask;
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.epilogue = epi;
+  g.dtype = dtype;
+  g.a_repeat = 1;
+  tfb::LnFuse ln = {ln_w, ln_b, eps, normed, ln_flags};
+  return tfb::gemm_splitk_f16(g, splits, static_cast<float*>(workspace), workspace_bytes, as_stream(stream), &ln);
 }
 
 int tf_flash_fwd(const void* q, const void* k, const void* v, int64_t ld_q, int64_t ld_kv, int64_t bs_q,

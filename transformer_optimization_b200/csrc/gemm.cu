@@ -837,6 +837,115 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const GemmArgs p) {
   }
 }
 
+// Split-K residual projection closed by the LayerNorm of its result, one
+// 128-thread block per row (4 consecutive columns per thread and chunk, NC4
+// chunks, so that a few-row input still spreads over many SMs):
+//   x_out  = mask_x(x_in + mask_delta(sum of the partials + bias))   (EPI 2;
+//            EPI 4 with the half-precision model's roundings to DT)
+//   normed = mask_out(LayerNorm(x_out) * w + b)
+// The partials are summed in split order, as splitk_reduce_kernel does, so
+// x_out is bit-identical to the unfused reduce; the moments are two-pass
+// (mean, then the centred sum of squares) as in the LayerNorm kernels. For
+// few-row inputs every kernel is latency-bound, and this saves the separate
+// LayerNorm launch of each residual site.
+constexpr int kRlnThreads = 128;
+
+__device__ __forceinline__ float block_sum_rln(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int warp = threadIdx.x >> 5;
+  __syncthreads();  // red is reused by consecutive reductions
+  if ((threadIdx.x & 31) == 0) red[warp] = v;
+  __syncthreads();
+  return (red[0] + red[1]) + (red[2] + red[3]);
+}
+
+template <int NC4, int EPI, int DT>
+__global__ void __launch_bounds__(kRlnThreads) splitk_reduce_ln_kernel(const GemmArgs p, const LnFuse ln) {
+  __shared__ float red[kRlnThreads / 32];
+  pdl_wait();
+  pdl_trigger();
+  const long long row = blockIdx.x;
+  const int N = p.N;
+  const long long plane = static_cast<long long>(p.M) * N;
+  const bool valid = p.valid == nullptr || p.valid[row] != 0;
+  float v[NC4][4];
+  float sum = 0.f;
+#pragma unroll
+  for (int i = 0; i < NC4; ++i) {
+    const int col = 4 * (static_cast<int>(threadIdx.x) + kRlnThreads * i);
+    if (col < N) {
+      const float* src = p.ws + row * N + col;
+      float4 a = *reinterpret_cast<const float4*>(src);
+#pragma unroll 4
+      for (int sp = 1; sp < p.splits; ++sp) {
+        const float4 b = *reinterpret_cast<const float4*>(src + sp * plane);
+        a.x += b.x; a.y += b.y; a.z += b.z; a.w += b.w;
+      }
+      const float4 q = __ldg(reinterpret_cast<const float4*>(p.bias + col));
+      const float d[4] = {a.x + q.x, a.y + q.y, a.z + q.z, a.w + q.w};
+      const long long off = row * p.ldx + col;
+      float x[4];
+      if constexpr (EPI == 4) {
+        const uint2 h = *reinterpret_cast<const uint2*>(p.x16_in + off);
+        const float2 f0 = unpack2<DT>(h.x), f1 = unpack2<DT>(h.y);
+        x[0] = f0.x; x[1] = f0.y; x[2] = f1.x; x[3] = f1.y;
+      } else {
+        const float4 x0 = *reinterpret_cast<const float4*>(p.x_in + off);
+        x[0] = x0.x; x[1] = x0.y; x[2] = x0.z; x[3] = x0.w;
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float dj = EPI == 4 ? round16<DT>(d[j]) : d[j];
+        if (p.mask_mode == 1 && !valid) dj = 0.f;
+        float y = x[j] + dj;
+        if constexpr (EPI == 4) y = round16<DT>(y);
+        if (p.mask_mode == 2 && !valid) y = 0.f;
+        v[i][j] = y;
+        sum += y;
+      }
+      if constexpr (EPI == 4) {
+        *reinterpret_cast<uint2*>(p.x16_out + off) = make_uint2(pack2<DT>(v[i][0], v[i][1]), pack2<DT>(v[i][2], v[i][3]));
+      } else {
+        *reinterpret_cast<float4*>(p.x_out + off) = make_float4(v[i][0], v[i][1], v[i][2], v[i][3]);
+      }
+    }
+  }
+  const float mean = block_sum_rln(sum, red) / static_cast<float>(N);
+  float sq = 0.f;
+#pragma unroll
+  for (int i = 0; i < NC4; ++i) {
+    if (4 * (static_cast<int>(threadIdx.x) + kRlnThreads * i) < N) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float dv = v[i][j] - mean;
+        sq += dv * dv;
+      }
+    }
+  }
+  const float rstd = rsqrtf(block_sum_rln(sq, red) / static_cast<float>(N) + ln.eps);
+  const bool zero_out = (ln.flags & TF_LN_MASK_OUT) && !valid;
+#pragma unroll
+  for (int i = 0; i < NC4; ++i) {
+    const int col = 4 * (static_cast<int>(threadIdx.x) + kRlnThreads * i);
+    if (col < N) {
+      const float4 wv = __ldg(reinterpret_cast<const float4*>(ln.w + col));
+      const float4 bv = __ldg(reinterpret_cast<const float4*>(ln.b + col));
+      const float wa[4] = {wv.x, wv.y, wv.z, wv.w}, ba[4] = {bv.x, bv.y, bv.z, bv.w};
+      float y[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) y[j] = zero_out ? 0.f : (v[i][j] - mean) * rstd * wa[j] + ba[j];
+      const long long off = row * N + col;
+      if (ln.flags & TF_LN_OUT_F32) {
+        *reinterpret_cast<float4*>(static_cast<float*>(ln.normed) + off) = make_float4(y[0], y[1], y[2], y[3]);
+      } else {
+        *reinterpret_cast<uint2*>(static_cast<uint16_t*>(ln.normed) + off) =
+            make_uint2(pack2<DT>(y[0], y[1]), pack2<DT>(y[2], y[3]));
+      }
+    }
+  }
+}
+
 // Split count and workspace bytes of a split-K call. splits <= 0: automatic,
 // about one work unit per two SMs and at least two k-blocks (128 of K) per
 // unit (measured on the small model configs: more splits only add partials
@@ -863,7 +972,8 @@ long long gemm_splitk_workspace_bytes(long long M, long long N, long long K, int
   return static_cast<long long>(splits) * M * N * 4;
 }
 
-int gemm_splitk_f16(const GemmCall& g, int splits_req, float* ws, long long ws_bytes, cudaStream_t stream) {
+int gemm_splitk_f16(const GemmCall& g, int splits_req, float* ws, long long ws_bytes, cudaStream_t stream,
+                    const LnFuse* ln) {
   const long long M = g.M, N = g.N, K = g.K;
   if (M <= 0 || N <= 0 || K <= 0) return set_error(TF_ERR_SHAPE, "gemm_splitk: empty shape M=%lld N=%lld K=%lld", M, N, K);
   if (M > (1ll << 31) - 1 || N > 65535ll * 64 || K > (1 << 24)) return set_error(TF_ERR_SHAPE, "gemm_splitk: shape out of range");
@@ -888,6 +998,18 @@ int gemm_splitk_f16(const GemmCall& g, int splits_req, float* ws, long long ws_b
     if (g.mask_mode != 0 && g.valid == nullptr) return set_error(TF_ERR_SHAPE, "gemm_splitk: mask without valid rows");
   } else if (g.C == nullptr || !aligned16(g.C) || g.ldc % 8 != 0 || g.ldc < N) {
     return set_error(TF_ERR_ALIGN, "gemm_splitk: C must be 16-byte aligned with a pitch >= N, multiple of 8");
+  }
+  if (ln != nullptr) {
+    if (g.epilogue != 2 && g.epilogue != 4)
+      return set_error(TF_ERR_SHAPE, "gemm_splitk: the fused LayerNorm follows a residual epilogue only");
+    if (N > 4096) return set_error(TF_ERR_SHAPE, "gemm_splitk: fused LayerNorm rows of %lld > 4096", N);
+    if (ln->w == nullptr || ln->b == nullptr || ln->normed == nullptr || !aligned16(ln->w) || !aligned16(ln->b) ||
+        !aligned16(ln->normed))
+      return set_error(TF_ERR_ALIGN, "gemm_splitk: LayerNorm weight, bias and output must be non-null, 16-byte aligned");
+    if (ln->flags & ~(TF_LN_MASK_OUT | TF_LN_OUT_F32))
+      return set_error(TF_ERR_SHAPE, "gemm_splitk: LayerNorm flags %d (TF_LN_MASK_OUT, TF_LN_OUT_F32)", ln->flags);
+    if ((ln->flags & TF_LN_MASK_OUT) && g.valid == nullptr)
+      return set_error(TF_ERR_SHAPE, "gemm_splitk: TF_LN_MASK_OUT without valid rows");
   }
   const int sms = device_sm_count();
   int splits, kps;
@@ -918,6 +1040,32 @@ int gemm_splitk_f16(const GemmCall& g, int splits_req, float* ws, long long ws_b
                           : launch_gemm_cfg<64, 8, 3, kDtF16>(ta, tb, args, grid, stream);
   if (rc) return rc;
 
+  if (ln != nullptr) {
+    // one block per row
+    const dim3 lgrid(static_cast<unsigned>(M));
+    const int n4 = static_cast<int>((N / 4 + kRlnThreads - 1) / kRlnThreads);
+    const int nc = n4 <= 1 ? 1 : n4 <= 2 ? 2 : n4 <= 4 ? 4 : 8;
+    cudaError_t e = cudaSuccess;
+#define TFB_RLN(C, E, D) e = launch_k(splitk_reduce_ln_kernel<C, E, D>, lgrid, dim3(kRlnThreads), 0, stream, args, *ln)
+#define TFB_RLN_NCH(E, D)                 \
+  switch (nc) {                           \
+    case 1: TFB_RLN(1, E, D); break;      \
+    case 2: TFB_RLN(2, E, D); break;      \
+    case 4: TFB_RLN(4, E, D); break;      \
+    default: TFB_RLN(8, E, D); break;     \
+  }
+    if (g.epilogue == 2) {
+      TFB_RLN_NCH(2, kDtF16)
+    } else if (g.dtype == kDtBF16) {
+      TFB_RLN_NCH(4, kDtBF16)
+    } else {
+      TFB_RLN_NCH(4, kDtF16)
+    }
+#undef TFB_RLN_NCH
+#undef TFB_RLN
+    if (e != cudaSuccess) return set_error(TF_ERR_LAUNCH, "gemm_splitk reduce+LayerNorm launch: %s", cudaGetErrorString(e));
+    return TF_OK;
+  }
   const long long nq = M * (N / 4);
   long long blocks = (nq + 255) / 256;
   if (blocks > 8ll * sms) blocks = 8ll * sms;

@@ -89,9 +89,21 @@ struct GemmCall {
   int pair;  // 0 automatic, 1 one-CTA tiles, 2 two-SM (CTA pair) tiles
 };
 
+// LayerNorm applied to the result of a residual projection (split-K form):
+// normed = mask_out(LayerNorm(x_out) * w + b), contiguous [M, N]
+struct LnFuse {
+  const float* w;
+  const float* b;
+  float eps;
+  void* normed;
+  int flags;  // TF_LN_MASK_OUT, TF_LN_OUT_F32
+};
+
 int gemm_f16(const GemmCall& g, cudaStream_t stream);
-// split-K GEMM (epilogues 0, 1, 2, 4, 5) with an fp32 partial-sum workspace
-int gemm_splitk_f16(const GemmCall& g, int splits, float* ws, long long ws_bytes, cudaStream_t stream);
+// split-K GEMM (epilogues 0, 1, 2, 4, 5) with an fp32 partial-sum workspace;
+// with `ln` (residual epilogues) the reduce kernel also runs that LayerNorm
+int gemm_splitk_f16(const GemmCall& g, int splits, float* ws, long long ws_bytes, cudaStream_t stream,
+                    const LnFuse* ln = nullptr);
 long long gemm_splitk_workspace_bytes(long long M, long long N, long long K, int splits);
 // the same with the library's fixed 4 MiB device scratch (no allocation)
 int gemm_splitk_static_f16(const GemmCall& g, int splits, cudaStream_t stream);

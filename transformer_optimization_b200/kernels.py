@@ -217,6 +217,57 @@ def linear_residual(a: torch.Tensor, w: torch.Tensor, b: torch.Tensor, x_in: tor
     return x_out
 
 
+def linear_residual_ln(a: torch.Tensor, w: torch.Tensor, b: torch.Tensor, x_in: torch.Tensor,
+                       x_out: Optional[torch.Tensor], valid: Optional[torch.Tensor], ln_weight: torch.Tensor,
+                       ln_bias: torch.Tensor, eps: float, *, mask_delta: bool = False, mask_x: bool = False,
+                       mask_out: bool = False, normed: Optional[torch.Tensor] = None,
+                       out_dtype: Optional[torch.dtype] = None, splits: int = 0,
+                       workspace: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Split-K residual projection whose reduce kernel also runs the
+    LayerNorm of the result (tf_gemm_residual_ln_splitk): x_out as
+    linear_residual, normed = mask_out(LayerNorm(x_out) * ln_weight +
+    ln_bias). normed is fp16 (fp32 x) or x's type (half x) unless out_dtype
+    is fp32. Returns (x_out, normed)."""
+    a2, n, k = _gemm_operands("linear_residual_ln", a, w, b, False)
+    _need_cuda("linear_residual_ln", x_in, x_out, valid, ln_weight, ln_bias, normed)
+    if x_in.dtype not in (torch.float32, a.dtype) or not x_in.is_contiguous() or x_in.shape[-1] != n:
+        raise ValueError("linear_residual_ln: x_in must be contiguous fp32 or a's type [..., N]")
+    if x_out is None:
+        x_out = torch.empty_like(x_in)
+    if x_out.shape != x_in.shape or x_out.dtype != x_in.dtype or not x_out.is_contiguous():
+        raise ValueError("linear_residual_ln: x_out must match x_in")
+    m = a2.shape[0]
+    if x_in.numel() // n != m:
+        raise ValueError("linear_residual_ln: row count of a and x differ")
+    if mask_delta and mask_x:
+        raise ValueError("linear_residual_ln: one mask mode at a time")
+    if ln_weight.dtype != torch.float32 or ln_bias.dtype != torch.float32 or ln_weight.numel() != n:
+        raise ValueError("linear_residual_ln: LayerNorm weight and bias must be fp32 [N]")
+    mode = _abi.TF_RES_MASK_DELTA if mask_delta else (_abi.TF_RES_MASK_X if mask_x else _abi.TF_RES_NO_MASK)
+    if (mode or mask_out) and (valid is None or valid.numel() != m or valid.dtype not in (torch.bool, torch.uint8)):
+        raise ValueError("linear_residual_ln: masking needs a bool/uint8 mask with one entry per row")
+    if valid is not None and not valid.is_contiguous():
+        valid = valid.contiguous()
+    half = x_in.dtype != torch.float32
+    if out_dtype is None:
+        out_dtype = x_in.dtype if half else torch.float16
+    if out_dtype not in (torch.float32, x_in.dtype if half else torch.float16):
+        raise ValueError("linear_residual_ln: out_dtype must be fp32 or the 16-bit type of the stream")
+    if normed is None:
+        normed = torch.empty(x_in.shape, dtype=out_dtype, device=x_in.device)
+    if normed.shape != x_in.shape or normed.dtype != out_dtype or not normed.is_contiguous():
+        raise ValueError("linear_residual_ln: normed must be contiguous, shaped like x, of out_dtype")
+    opts = (_abi.TF_RES_X16 if half else 0) | (_abi.TF_RES_BF16 if a.dtype == torch.bfloat16 else 0)
+    ln_flags = (_abi.TF_LN_MASK_OUT if mask_out else 0) | (_abi.TF_LN_OUT_F32 if out_dtype == torch.float32 else 0)
+    ws = _splitk_ws(workspace, m, n, k, splits, a.device)
+    use_valid = mode or mask_out
+    _abi.call("tf_gemm_residual_ln_splitk", _ptr(a2), a2.stride(0), _ptr(w), w.stride(0), _ptr(b), _ptr(x_in),
+              _ptr(x_out), n, _ptr(valid) if use_valid else None, mode | opts, m, n, k, int(splits), _ptr(ws),
+              ws.numel() * ws.element_size(), _ptr(ln_weight), _ptr(ln_bias), float(eps), _ptr(normed), ln_flags,
+              _stream())
+    return x_out, normed
+
+
 def flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, heads: int, scale: float, *,
                     causal: bool = False, key_valid: Optional[torch.Tensor] = None, q_pos0: int = 0,
                     k_pos0: int = 0, out: Optional[torch.Tensor] = None, out_dtype: Optional[torch.dtype] = None,

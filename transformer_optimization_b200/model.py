@@ -270,23 +270,47 @@ class UserOptimizedTransformer(BaselineTransformer):
             if ws is None or ws.device != dev or ws.numel() < need:
                 ws = self._splitk_ws = torch.empty(need, dtype=torch.uint8, device=dev)
 
+        # With split-K residual projections (few rows), their reduce kernel also
+        # runs the LayerNorm that follows (the next layer's norm1, or the final
+        # norm after the last layer): one launch fewer per residual site.
         cur = x  # residual stream; the caller's x is read, never written
+        out = None
+        normed_ready = False  # normed already holds this layer's norm1 output
+        n_layers = len(self.layers)
         for li, blk in enumerate(self.layers):
             w = wts[li]
-            kernels.ln_residual(cur, None, w.n1w, w.n1b, blk.norm1.eps, normed=normed)
+            if not normed_ready:
+                kernels.ln_residual(cur, None, w.n1w, w.n1b, blk.norm1.eps, normed=normed)
             kernels.linear(normed, w.wqkv, w.bqkv, out=qkv, splits=sk_qkv, workspace=ws)
             kernels.flash_attention(qkv[..., :d], qkv[..., d:2 * d], qkv[..., 2 * d:], h, scale,
                                     causal=cfg.causal, key_valid=kvalid, out=ctx)
-            cur = kernels.linear_residual(ctx, w.wo, w.bo, cur, x_res, vflat, mask_delta=mask_active,
-                                          splits=sk_o, workspace=ws)
-            kernels.ln_residual(cur, None, w.n2w, w.n2b, blk.norm2.eps, normed=normed)
+            if sk_o is not None:
+                cur, _ = kernels.linear_residual_ln(ctx, w.wo, w.bo, cur, x_res, vflat, w.n2w, w.n2b,
+                                                    blk.norm2.eps, mask_delta=mask_active, normed=normed,
+                                                    splits=sk_o, workspace=ws)
+            else:
+                cur = kernels.linear_residual(ctx, w.wo, w.bo, cur, x_res, vflat, mask_delta=mask_active)
+                kernels.ln_residual(cur, None, w.n2w, w.n2b, blk.norm2.eps, normed=normed)
             kernels.linear(normed, w.w1, w.b1, gelu=True, out=hidden, splits=sk_1, workspace=ws,
                            round_gelu_input=half)
-            kernels.linear_residual(hidden, w.w2, w.b2, cur, x_res, vflat, mask_x=mask_active,
-                                    w_split=w.split_w2, splits=sk_2, workspace=ws)
-        fw, fb = self._final_ln
-        _, out = kernels.ln_residual(cur, None, fw, fb, self.final_norm.eps, vflat, mask_out=mask_active,
-                                     out_dtype=x.dtype)
+            if sk_2 is None:
+                kernels.linear_residual(hidden, w.w2, w.b2, cur, x_res, vflat, mask_x=mask_active,
+                                        w_split=w.split_w2)
+                normed_ready = False
+            elif li + 1 < n_layers:
+                wn, nxt = wts[li + 1], self.layers[li + 1]
+                kernels.linear_residual_ln(hidden, w.w2, w.b2, cur, x_res, vflat, wn.n1w, wn.n1b, nxt.norm1.eps,
+                                           mask_x=mask_active, normed=normed, splits=sk_2, workspace=ws)
+                normed_ready = True
+            else:
+                fw, fb = self._final_ln
+                _, out = kernels.linear_residual_ln(hidden, w.w2, w.b2, cur, x_res, vflat, fw, fb,
+                                                    self.final_norm.eps, mask_x=mask_active, mask_out=mask_active,
+                                                    out_dtype=x.dtype, splits=sk_2, workspace=ws)
+        if out is None:
+            fw, fb = self._final_ln
+            _, out = kernels.ln_residual(cur, None, fw, fb, self.final_norm.eps, vflat, mask_out=mask_active,
+                                         out_dtype=x.dtype)
         return out
 
     # ------------------------------------------------------------------ graphs
