@@ -146,3 +146,52 @@ def test_bench_algorithmic_bytes():
               + 2 * (m * d + d * d) + 8 * m * d + 2 * (m * f + d * f) + 8 * m * d) / 4
     assert bench.algo_bytes_per_gemm(cfg) == expect
     assert 140e6 < bench.C3_GEMM_DRAM_BYTES_PER_LAUNCH < expect  # measured DRAM bytes below algorithmic
+
+
+def _record_schedule(monkeypatch, cfg, m_rows):
+    """Run the model's per-layer schedule with the kernel wrappers replaced
+    by recorders (no GPU): returns [(wrapper, kwargs)] in call order."""
+    import types
+    from transformer_optimization_b200 import kernels as K
+    calls = []
+
+    def rec(name, ret):
+        def f(*a, **kw):
+            calls.append((name, kw))
+            return ret(*a, **kw)
+        return f
+
+    monkeypatch.setattr(torch.cuda, "get_device_properties",
+                        lambda dev: types.SimpleNamespace(multi_processor_count=148))
+    monkeypatch.setattr(K, "splitk_workspace_bytes", lambda m, n, k, splits=0: 1024)
+    monkeypatch.setattr(K, "ln_residual", rec("ln", lambda x, *a, **kw: (x, torch.zeros(1))))
+    monkeypatch.setattr(K, "linear", rec("linear", lambda *a, **kw: None))
+    monkeypatch.setattr(K, "flash_attention", rec("flash", lambda *a, **kw: (None, None)))
+    monkeypatch.setattr(K, "linear_residual", rec("res", lambda a, w, b, x_in, x_out, *r, **kw: x_out))
+    monkeypatch.setattr(K, "linear_residual_ln",
+                        rec("res_ln", lambda a, w, b, x_in, x_out, *r, **kw: (x_out, torch.zeros(1))))
+    model = UserOptimizedTransformer(cfg)
+    model._forward_core(torch.zeros(1, m_rows, cfg.d_model), None, False)
+    return calls
+
+
+def test_forward_schedule_few_rows(monkeypatch):
+    """c2 (64 rows): every projection takes the split-K form and each
+    residual site runs the following LayerNorm in its reduce kernel (the next
+    layer's norm1, the final norm after the last layer, fp32 out)."""
+    cfg = NAMED_CONFIGS["c2"]
+    calls = _record_schedule(monkeypatch, cfg, 64)
+    names = [c[0] for c in calls]
+    assert names == ["ln"] + ["linear", "flash", "res_ln", "linear", "res_ln"] * cfg.num_layers
+    assert all(kw.get("splits") == 0 for n, kw in calls if n in ("linear", "res_ln"))
+    assert calls[-1][1]["out_dtype"] == torch.float32 and calls[-1][1]["mask_out"] is False
+
+
+def test_forward_schedule_many_rows(monkeypatch):
+    """c3-sized rows: no split-K; residual sites in the GEMM epilogue, then a
+    LayerNorm kernel each, and the final LayerNorm."""
+    cfg = TransformerConfig(8, 2048, 1024, 16, 4096, 2, False)
+    calls = _record_schedule(monkeypatch, cfg, 8 * 2048)  # the 16 384 rows as one sequence
+    names = [c[0] for c in calls]
+    assert names == ["ln", "linear", "flash", "res", "ln", "linear", "res"] * cfg.num_layers + ["ln"]
+    assert all(kw.get("splits") is None for n, kw in calls if n == "linear")
