@@ -103,15 +103,6 @@ __device__ __forceinline__ float ex2_f32(float x) {
   return y;
 }
 
-// 2^a, 2^b for a pair, through the packed half-precision unit: returns the
-// fp16 pair {2^a (low), 2^b (high)}.
-__device__ __forceinline__ uint32_t ex2_pair_f16(float a, float b) {
-  uint32_t h, r;
-  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(b), "f"(a));
-  asm("ex2.approx.f16x2 %0, %1;" : "=r"(r) : "r"(h));
-  return r;
-}
-
 __device__ __forceinline__ float fmax3f(float a, float b, float c) {
   float d;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
