@@ -195,3 +195,38 @@ def test_forward_schedule_many_rows(monkeypatch):
     names = [c[0] for c in calls]
     assert names == ["ln", "linear", "flash", "res", "ln", "linear", "res"] * cfg.num_layers + ["ln"]
     assert all(kw.get("splits") is None for n, kw in calls if n == "linear")
+
+
+C_PROGRAM = r"""
+#include <stdio.h>
+#include <string.h>
+#include "tfb200.h"
+
+int main(void) {
+  printf("abi %d\n", tf_abi_version());
+  /* null operands: refused with a status code and a message, whether or not
+     a GPU is present (no device: TF_ERR_DEVICE; device: a shape/alignment code) */
+  int rc = tf_gemm(NULL, 64, NULL, 64, NULL, NULL, 64, 64, 64, 64, TF_EPI_BIAS, NULL);
+  const char* msg = tf_last_error();
+  printf("rc %d msg_len %d\n", rc, (int)strlen(msg));
+  return (rc != TF_OK && strlen(msg) > 0) ? 0 : 1;
+}
+"""
+
+
+def test_c_program_binds_the_abi(lib, tmp_path):
+    """The header is plain C: a C program compiled by gcc against
+    include/tfb200.h links libtfb200.so and gets a refused call's status code
+    and message (the binding a C, cgo or other FFI host would use)."""
+    import shutil
+    if shutil.which("gcc") is None:
+        pytest.skip("gcc not available")
+    src = tmp_path / "abi_smoke.c"
+    src.write_text(C_PROGRAM)
+    exe = tmp_path / "abi_smoke"
+    libdir = _abi.LIB_PATH.parent
+    subprocess.run(["gcc", "-std=c99", "-Wall", "-Werror", "-I", str(ROOT / "include"), str(src), "-o", str(exe),
+                    f"-L{libdir}", "-l:libtfb200.so", f"-Wl,-rpath,{libdir}"], check=True, capture_output=True)
+    res = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
+    assert res.returncode == 0, res.stdout + res.stderr
+    assert f"abi {lib.tf_abi_version()}" in res.stdout
