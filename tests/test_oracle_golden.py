@@ -123,3 +123,36 @@ def test_query_tiled_equals_dense():
     y0 = om.forward(p, cfg, x)
     y1 = om.forward(p, cfg, x, query_tile=16, ffn_row_chunk=33)
     assert torch.allclose(y0, y1, atol=1e-5)
+
+
+@pytest.mark.parametrize("dt", [torch.float16, torch.bfloat16], ids=["fp16", "bf16"])
+def test_half_helpers_match_eager_ops(dt):
+    """The oracle's per-kernel statements for half-precision models
+    (linear_half, linear_residual_half, ln_site_half) agree with the eager ops
+    the reference's model runs in that type (nn.Linear, F.gelu, the residual
+    add, nn.LayerNorm on T tensors, torch_transformer_benchmark.py:162-248) on
+    the CPU: within two ulps of T (ATen accumulates in fp32, the oracle
+    exactly)."""
+    import torch.nn.functional as F
+    g = torch.Generator().manual_seed(5)
+    ulp = 2.0 ** -10 if dt == torch.float16 else 2.0 ** -7
+    a = torch.randn(48, 96, generator=g).to(dt)
+    w = (torch.randn(64, 96, generator=g) * 96 ** -0.5).to(dt)
+    b = (torch.randn(64, generator=g) * 0.1).to(dt)
+    x = (torch.randn(48, 64, generator=g) * 2).to(dt)
+    lw = (torch.randn(64, generator=g) * 0.1 + 1).to(dt)
+    lb = (torch.randn(64, generator=g) * 0.1).to(dt)
+
+    def close(got, want):
+        want = want.float()
+        assert torch.all((got.float() - want).abs() <= 2 * ulp * want.abs() + 1e-6)
+
+    h = F.linear(a, w, b)
+    close(om.linear_half(a, w, b.float(), False, dt), h)
+    close(om.linear_half(a, w, b.float(), True, dt), F.gelu(h, approximate="none"))
+    x_new, _ = om.linear_residual_half(a, w, b.float(), x, None, False, False, dt)
+    close(x_new, x + h)
+    delta = (torch.randn(48, 64, generator=g) * 0.5).to(dt)
+    xs, y = om.ln_site_half(x, delta, lw.float(), lb.float(), 1e-5, None, False, False, False, dt)
+    assert torch.equal(xs, (x + delta).float())
+    close(y.to(dt), F.layer_norm(x + delta, (64,), lw, lb, 1e-5))
