@@ -148,7 +148,7 @@ def test_bench_algorithmic_bytes():
     assert 140e6 < bench.C3_GEMM_DRAM_BYTES_PER_LAUNCH < expect  # measured DRAM bytes below algorithmic
 
 
-def _record_schedule(monkeypatch, cfg, m_rows):
+def _record_schedule(monkeypatch, cfg, m_rows, chunk_budget=None):
     """Run the model's per-layer schedule with the kernel wrappers replaced
     by recorders (no GPU): returns [(wrapper, kwargs)] in call order."""
     import types
@@ -162,7 +162,8 @@ def _record_schedule(monkeypatch, cfg, m_rows):
         return f
 
     monkeypatch.setattr(torch.cuda, "get_device_properties",
-                        lambda dev: types.SimpleNamespace(multi_processor_count=148))
+                        lambda dev: types.SimpleNamespace(multi_processor_count=148,
+                                                          total_memory=183359 * 2**20))
     monkeypatch.setattr(K, "splitk_workspace_bytes", lambda m, n, k, splits=0: 1024)
     monkeypatch.setattr(K, "ln_residual", rec("ln", lambda x, *a, **kw: (x, torch.zeros(1))))
     monkeypatch.setattr(K, "linear", rec("linear", lambda *a, **kw: None))
@@ -171,6 +172,7 @@ def _record_schedule(monkeypatch, cfg, m_rows):
     monkeypatch.setattr(K, "linear_residual_ln",
                         rec("res_ln", lambda a, w, b, x_in, x_out, *r, **kw: (x_out, torch.zeros(1))))
     model = UserOptimizedTransformer(cfg)
+    model.ffn_chunk_budget_bytes = chunk_budget
     model._forward_core(torch.zeros(1, m_rows, cfg.d_model), None, False)
     return calls
 
@@ -195,6 +197,34 @@ def test_forward_schedule_many_rows(monkeypatch):
     names = [c[0] for c in calls]
     assert names == ["ln", "linear", "flash", "res", "ln", "linear", "res"] * cfg.num_layers + ["ln"]
     assert all(kw.get("splits") is None for n, kw in calls if n == "linear")
+
+
+def test_ffn_chunk_decision():
+    """The FFN runs in row chunks only when the [rows, ffn_dim] hidden would
+    exceed the budget (torch_transformer_benchmark.py:3886-3908): chunks
+    are a power of two of rows that fits, at least 256, at most all rows."""
+    from transformer_optimization_b200.model import FFN_CHUNK_BUDGET_FRAC, ffn_chunk_rows
+    b200 = int(183359 * 2**20 * FFN_CHUNK_BUDGET_FRAC)
+    for name in ("c1", "c2", "c3", "c4", "c5"):  # BASELINE's configs never chunk on a B200
+        c = NAMED_CONFIGS[name]
+        assert ffn_chunk_rows(c.batch_size * c.seq_len, c.ffn_dim, 2, b200) is None
+    assert ffn_chunk_rows(1000, 1024, 2, 300 * 1024 * 2) == 256
+    assert ffn_chunk_rows(1000, 1024, 2, 600 * 1024 * 2) == 512
+    assert ffn_chunk_rows(1000, 1024, 2, 10) == 256          # floor
+    assert ffn_chunk_rows(200, 1024, 2, 10) == 200           # never more than the rows
+    assert ffn_chunk_rows(1000, 1024, 2, 1000 * 1024 * 2) is None
+    # the reference's row-14 shape on a 16 GB card would chunk; on a B200 it does not
+    assert ffn_chunk_rows(32 * 100000, 1024, 2, b200) is None
+    assert ffn_chunk_rows(32 * 100000, 1024, 2, int(16e9 * FFN_CHUNK_BUDGET_FRAC)) == 1 << 20
+
+
+def test_forward_schedule_chunked_ffn(monkeypatch):
+    """Over budget: each layer's FFN becomes FFN-in + FFN-out per row chunk,
+    in place on the residual stream, followed by the next LayerNorm site."""
+    cfg = TransformerConfig(1, 1000, 256, 4, 1024, 2, False)
+    calls = _record_schedule(monkeypatch, cfg, 1000, chunk_budget=300 * 1024 * 2)
+    names = [c[0] for c in calls]
+    assert names == (["ln", "linear", "flash", "res", "ln"] + ["linear", "res"] * 4) * cfg.num_layers + ["ln"]
 
 
 C_PROGRAM = r"""

@@ -93,6 +93,58 @@ def test_all_true_mask_and_graph_replay():
     _check(om.forward(p, cfg, x), a)
 
 
+def test_graphs_keep_their_splitk_workspace():
+    """Two few-row shapes captured one after the other: the second needs a
+    larger split-K workspace, which replaces the model's current one. The
+    first graph must keep replaying into the workspace it was captured with,
+    never into memory the allocator has since handed to another tensor."""
+    cfg = NAMED_CONFIGS["c2"]
+    p, _, model = _build(cfg)
+    g = torch.Generator().manual_seed(5)
+    x_small = torch.randn(1, 32, cfg.d_model, generator=g).cuda()
+    x_big = torch.randn(2, 64, cfg.d_model, generator=g).cuda()
+    with torch.inference_mode():
+        a1 = model(x_small)
+        ws_small = model._splitk_ws
+        b1 = model(x_big)
+        assert model._splitk_ws is not ws_small and model._splitk_ws.numel() > ws_small.numel()
+        n_small = ws_small.numel()
+        del ws_small
+        # tensors of the old workspace's size: if it had been freed, one of
+        # them would now sit on its memory
+        sentinels = [torch.full((n_small,), 7, dtype=torch.uint8, device="cuda") for _ in range(8)]
+        a2 = model(x_small)
+        b2 = model(x_big)
+        torch.cuda.synchronize()
+    for s in sentinels:
+        assert bool((s == 7).all()), "a graph replay wrote into memory it does not own"
+    assert torch.equal(a1, a2) and torch.equal(b1, b2)
+    small_cfg = TransformerConfig(1, 32, cfg.d_model, cfg.num_heads, cfg.ffn_dim, cfg.num_layers, cfg.causal)
+    big_cfg = TransformerConfig(2, 64, cfg.d_model, cfg.num_heads, cfg.ffn_dim, cfg.num_layers, cfg.causal)
+    _check(om.forward(p, small_cfg, x_small.cpu()), a2)
+    _check(om.forward(p, big_cfg, x_big.cpu()), b2)
+
+
+@pytest.mark.parametrize("masked", [False, True])
+def test_chunked_ffn_is_bit_identical(masked):
+    """With the FFN budget forced low, the FFN runs over row chunks (256, 256,
+    256, 232 rows); every GEMM row is computed the same way whatever the row
+    count, so the output equals the unchunked forward bit for bit, and both
+    pass the gate against the oracle."""
+    cfg = TransformerConfig(2, 500, 256, 4, 1024, 2, False)
+    p, x, model = _build(cfg, seed=3)
+    mask = om.padded_mask(cfg, 0.3, 11) if masked else None
+    if masked:
+        x = x.masked_fill(~mask[..., None], 0)
+    xg, mg = x.cuda(), (mask.cuda() if masked else None)
+    with torch.inference_mode():
+        whole = model(xg, mg)
+        model.ffn_chunk_budget_bytes = 300 * cfg.ffn_dim * 2
+        chunked = model(xg, mg)
+    assert torch.equal(whole, chunked)
+    _check(om.forward(p, cfg, x, mask), chunked)
+
+
 def test_weight_reload_invalidates_caches():
     cfg = NAMED_CONFIGS["c1"]
     p, x, model = _build(cfg)

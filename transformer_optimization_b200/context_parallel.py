@@ -3,18 +3,35 @@
 The reference has no multi-GPU code; for sequences too long for one device it
 streams shards through host memory (torch_transformer_benchmark.py:4400-4531,
 4686-4771). Here the sequence stays resident and is split over GPUs instead:
-rank r owns the contiguous token range `shard_bounds(S, n)[r]` and runs every
-token-wise op (LayerNorm, the four GEMMs, GELU, residual adds) on its own
-rows. Attention is the one exchange step: a ring.
+each rank owns one or more token segments of the global sequence (its
+"layout" entry) and runs every token-wise op (LayerNorm, the four GEMMs,
+GELU, residual adds) on its own rows. Attention is the one exchange step: a
+ring.
+
+Layouts (per rank: a list of (global start, length) segments, concatenated
+in that order into the rank's local rows):
+  * contiguous: rank r owns shard_bounds(S, n)[r] (non-causal attention costs
+    the same on every rank);
+  * zigzag: the sequence is cut into 2n chunks and rank r owns chunks r and
+    2n-1-r, so under a causal mask every rank has the same amount of work
+    (with contiguous shards rank r would compute r+1 of the n key blocks).
 
 Ring attention (per layer). Each rank packs its K|V rows into a contiguous
-buffer; for step t = 0 .. n-1 it holds the K|V block that started on rank
-(r - t) mod n, computes flash attention of its queries against that block
-(global token positions make the causal mask exact), and merges the partial
-result into its running (O, lse) by log-sum-exp. While step t computes, the
-block moves one hop (send to r+1, receive from r-1) into the second buffer,
-so the NVLink transfer overlaps the tensor-core work. Remote blocks land in
-this GPU's own memory before any kernel reads them.
+buffer; for step t = 0 .. n-1 it holds the K|V rows that started on rank
+(r - t) mod n, computes flash attention of each of its query segments
+against each key segment of that block (global token positions make the
+causal mask exact; a segment pair entirely above the diagonal is skipped),
+and merges each partial result into the running (O, lse) of its query
+segment by log-sum-exp. While step t computes, the block moves one hop (send
+to r+1, receive from r-1) into the second buffer, so the NVLink transfer
+overlaps the tensor-core work. Remote blocks land in this GPU's own memory
+before any kernel reads them. The buffers are kept across layers and calls.
+
+Failure handling: ranks that stop answering make their peers fail instead of
+hanging. With `deadline_s` set, the host waits at most that long for each
+forward's ring (CPU tensors: every exchange; CUDA tensors: the end of the
+forward, by polling an event) and then aborts the group's communicators and
+raises RingTimeout. Without it the process group's own timeout applies.
 
 The attention arithmetic is behind a small backend interface: the product
 uses `CudaAttentionBackend` (the sm_100a flash and merge kernels); the CPU
@@ -23,15 +40,24 @@ tests drive the same ring over gloo with a host backend.
 
 from __future__ import annotations
 
-from typing import List, Optional, Sequence, Tuple
+import datetime
+import time
+from typing import Dict, List, Optional, Sequence, Tuple
 
 import torch
 import torch.distributed as dist
 
 from . import kernels
 
+Segment = Tuple[int, int]
 
-def shard_bounds(seq_len: int, world: int) -> List[Tuple[int, int]]:
+
+class RingTimeout(RuntimeError):
+    """A ring exchange did not complete within the host deadline; the
+    group's communicators have been aborted."""
+
+
+def shard_bounds(seq_len: int, world: int) -> List[Segment]:
     """Contiguous (start, length) per rank; the first seq_len % world ranks
     get one extra token."""
     base, rem = divmod(seq_len, world)
@@ -43,23 +69,73 @@ def shard_bounds(seq_len: int, world: int) -> List[Tuple[int, int]]:
     return out
 
 
+def contiguous_layout(seq_len: int, world: int) -> List[List[Segment]]:
+    return [[b] for b in shard_bounds(seq_len, world)]
+
+
+def zigzag_layout(seq_len: int, world: int) -> List[List[Segment]]:
+    """2*world chunks (shard_bounds of the sequence over 2*world); rank r owns
+    chunks r and 2*world-1-r, in that order."""
+    chunks = shard_bounds(seq_len, 2 * world)
+    return [[chunks[r], chunks[2 * world - 1 - r]] for r in range(world)]
+
+
+def as_layout(bounds_or_layout) -> List[List[Segment]]:
+    """Accept either a per-rank list of (start, length) (contiguous shards)
+    or a per-rank list of segment lists."""
+    out = []
+    for entry in bounds_or_layout:
+        if len(entry) == 2 and all(isinstance(v, int) for v in entry):
+            out.append([(int(entry[0]), int(entry[1]))])
+        else:
+            out.append([(int(s), int(n)) for s, n in entry])
+    return out
+
+
+def local_length(segments: Sequence[Segment]) -> int:
+    return sum(n for _, n in segments)
+
+
+def local_positions(segments: Sequence[Segment]) -> torch.Tensor:
+    """Global token index of each local row."""
+    return torch.cat([torch.arange(s, s + n) for s, n in segments]) if segments else torch.zeros(0, dtype=torch.long)
+
+
+def causal_work(layout: Sequence[Sequence[Segment]]) -> List[int]:
+    """Query-key pairs each rank evaluates under a causal mask (for load
+    balance checks): sum over its query tokens of (global position + 1)."""
+    return [sum((s + n) * (s + n + 1) // 2 - s * (s + 1) // 2 for s, n in segs) for segs in layout]
+
+
 def ring_sources(rank: int, world: int) -> List[int]:
     """Origin rank of the K/V block a rank holds at each ring step."""
     return [(rank - t) % world for t in range(world)]
 
 
 class CudaAttentionBackend:
-    """Block attention and merge on the B200 kernels."""
+    """Block attention and merge on the B200 kernels. With `timeline` set to
+    a list, every merge launch is bracketed by CUDA events on the current
+    stream and recorded as ("merge", start, end)."""
 
-    def block(self, q, k, v, heads, scale, causal, q_pos0, k_pos0, key_valid, first, o_acc, lse_acc,
-              o_part, lse_part):
+    def __init__(self):
+        self.timeline: Optional[list] = None
+
+    def block(self, q, k, v, heads, scale, causal, q_pos0, k_pos0, key_valid, first, o_acc, lse_acc, o_part,
+              lse_part):
         if first:
             kernels.flash_attention(q, k, v, heads, scale, causal=causal, key_valid=key_valid, q_pos0=q_pos0,
                                     k_pos0=k_pos0, out=o_acc, out_dtype=torch.float32, lse=lse_acc)
         else:
             kernels.flash_attention(q, k, v, heads, scale, causal=causal, key_valid=key_valid, q_pos0=q_pos0,
                                     k_pos0=k_pos0, out=o_part, out_dtype=torch.float32, lse=lse_part)
-            kernels.attn_merge(o_acc, lse_acc, o_part, lse_part, heads)
+            if self.timeline is not None:
+                s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                s.record()
+                kernels.attn_merge(o_acc, lse_acc, o_part, lse_part, heads)
+                e.record()
+                self.timeline.append(("merge", s, e))
+            else:
+                kernels.attn_merge(o_acc, lse_acc, o_part, lse_part, heads)
 
     def finish(self, o_acc, out16):
         out16.copy_(o_acc)
@@ -69,56 +145,125 @@ class RingAttention:
     """Ring attention over `group` (all ranks call it together, same shapes
     except the local sequence length)."""
 
-    def __init__(self, group=None, backend=None):
+    def __init__(self, group=None, backend=None, deadline_s: Optional[float] = None):
         self.group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
         self.backend = backend if backend is not None else CudaAttentionBackend()
+        self.deadline_s = deadline_s
         self._peer_next = dist.get_global_rank(group, (self.rank + 1) % self.world) if group else (self.rank + 1) % self.world
         self._peer_prev = dist.get_global_rank(group, (self.rank - 1) % self.world) if group else (self.rank - 1) % self.world
+        self._buffers: Dict[Tuple, Tuple] = {}
+        # with a list here, each ring step's block computation and exposed
+        # exchange wait are bracketed by CUDA events: ("block", s, e),
+        # ("wait", s, e) (and the backend's ("merge", s, e))
+        self.timeline: Optional[list] = None
+        self._t_deadline: Optional[float] = None
+
+    def _get_buffers(self, b, s_max, s_loc, d, heads, seg_lens, dt, dev):
+        key = (b, s_max, s_loc, d, heads, tuple(seg_lens), dt, dev)
+        bufs = self._buffers.get(key)
+        if bufs is None:
+            n = self.world
+            kv = [torch.empty(b, s_max, 2 * d, dtype=dt, device=dev) for _ in range(2 if n > 1 else 1)]
+            o_acc = torch.empty(b, s_loc, d, dtype=torch.float32, device=dev)
+            o_part = torch.empty_like(o_acc)
+            lse_acc = [torch.empty(b, heads, L, dtype=torch.float32, device=dev) for L in seg_lens]
+            lse_part = [torch.empty_like(t) for t in lse_acc]
+            self._buffers.clear()  # one shape at a time
+            bufs = self._buffers[key] = (kv, o_acc, o_part, lse_acc, lse_part)
+        return bufs
+
+    def _wait(self, reqs, on_cuda: bool) -> None:
+        """Complete this step's exchange. CUDA tensors: the current stream
+        waits for it (no host block). CPU tensors with a deadline: the host
+        waits at most until the deadline, then aborts and raises."""
+        for r in reqs:
+            if self._t_deadline is not None and not on_cuda:
+                left = self._t_deadline - time.monotonic()
+                try:
+                    r.wait(datetime.timedelta(seconds=max(left, 0.001)))
+                except Exception as exc:
+                    self.abort()
+                    raise RingTimeout(f"rank {self.rank}: ring exchange not done within {self.deadline_s} s "
+                                      f"({exc})") from exc
+            else:
+                r.wait()
+
+    def abort(self) -> None:
+        """Abort the group's communicators (ends any exchange still pending
+        on them); the group cannot be used afterwards."""
+        try:
+            dist.distributed_c10d._abort_process_group(self.group)
+        except Exception:
+            pass
 
     def __call__(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, heads: int, scale: float,
-                 causal: bool, bounds: Sequence[Tuple[int, int]], out16: torch.Tensor,
+                 causal: bool, layout, out16: torch.Tensor,
                  key_valid_full: Optional[torch.Tensor] = None) -> torch.Tensor:
-        """q, k, v: this rank's [B, S_loc, D] (any pitch, unit inner stride);
-        bounds: shard_bounds of the full sequence; out16: [B, S_loc, D]
-        receives the attention output; key_valid_full: bool [B, S] or None."""
+        """q, k, v: this rank's [B, S_loc, D] (any pitch, unit inner stride),
+        rows in the order of this rank's segments; layout: per-rank segment
+        lists (or contiguous shard_bounds); out16: [B, S_loc, D] receives the
+        attention output; key_valid_full: bool [B, S] or None."""
+        layout = as_layout(layout)
         b, s_loc, d = q.shape
         n = self.world
-        s_max = max(length for _, length in bounds)
+        segs = layout[self.rank]
+        if local_length(segs) != s_loc:
+            raise ValueError(f"rank {self.rank}: {s_loc} local rows but the layout gives {local_length(segs)}")
+        s_max = max(local_length(r) for r in layout)
         dev = q.device
-        dt = k.dtype
-        # contiguous K|V send/receive buffers (double buffered)
-        bufs = [torch.empty(b, s_max, 2 * d, dtype=dt, device=dev) for _ in range(2 if n > 1 else 1)]
-        bufs[0][:, :s_loc, :d].copy_(k)
-        bufs[0][:, :s_loc, d:].copy_(v)
-        o_acc = torch.empty(b, s_loc, d, dtype=torch.float32, device=dev)
-        lse_acc = torch.empty(b, heads, s_loc, dtype=torch.float32, device=dev)
-        o_part = torch.empty_like(o_acc) if n > 1 else None
-        lse_part = torch.empty_like(lse_acc) if n > 1 else None
-        q_pos0 = bounds[self.rank][0]
-        q_last = q_pos0 + s_loc - 1
-        first = True
+        seg_lens = [length for _, length in segs]
+        kv, o_acc, o_part, lse_acc, lse_part = self._get_buffers(b, s_max, s_loc, d, heads, seg_lens, k.dtype, dev)
+        kv[0][:, :s_loc, :d].copy_(k)
+        kv[0][:, :s_loc, d:].copy_(v)
+        if self.deadline_s is not None:
+            self._t_deadline = time.monotonic() + self.deadline_s
+        q_off = [0]
+        for length in seg_lens:
+            q_off.append(q_off[-1] + length)
+        o_acc_v = [o_acc[:, q_off[i]:q_off[i + 1]] for i in range(len(segs))]
+        o_part_v = [o_part[:, q_off[i]:q_off[i + 1]] for i in range(len(segs))]
+        first = [True] * len(segs)
+        tl = self.timeline
+        if hasattr(self.backend, "timeline"):
+            self.backend.timeline = tl
         for t, src in enumerate(ring_sources(self.rank, n)):
-            cur = bufs[t % 2]
+            cur = kv[t % 2]
             reqs = []
             if t < n - 1:
                 ops = [dist.P2POp(dist.isend, cur, self._peer_next, self.group),
-                       dist.P2POp(dist.irecv, bufs[(t + 1) % 2], self._peer_prev, self.group)]
+                       dist.P2POp(dist.irecv, kv[(t + 1) % 2], self._peer_prev, self.group)]
                 reqs = dist.batch_isend_irecv(ops)
-            k_pos0, k_len = bounds[src]
-            skip = k_len == 0 or (causal and k_pos0 > q_last)
-            if not skip:
-                kv_mask = None
-                if key_valid_full is not None:
-                    kv_mask = key_valid_full[:, k_pos0:k_pos0 + k_len]
-                self.backend.block(q, cur[:, :k_len, :d], cur[:, :k_len, d:], heads, scale, causal, q_pos0, k_pos0,
-                                   kv_mask, first, o_acc, lse_acc, o_part, lse_part)
-                first = False
-            for r in reqs:
-                r.wait()
-        if first:  # every key of every block was masked for these queries
-            o_acc.zero_()
+            if tl is not None:
+                ev0 = torch.cuda.Event(enable_timing=True)
+                ev0.record()
+            k_off = 0
+            for k_pos0, k_len in layout[src]:
+                if k_len == 0:
+                    continue
+                kk = cur[:, k_off:k_off + k_len, :d]
+                vv = cur[:, k_off:k_off + k_len, d:]
+                kv_mask = key_valid_full[:, k_pos0:k_pos0 + k_len] if key_valid_full is not None else None
+                for i, (q_pos0, q_len) in enumerate(segs):
+                    if q_len == 0 or (causal and k_pos0 > q_pos0 + q_len - 1):
+                        continue
+                    self.backend.block(q[:, q_off[i]:q_off[i + 1]], kk, vv, heads, scale, causal, q_pos0, k_pos0,
+                                       kv_mask, first[i], o_acc_v[i], lse_acc[i], o_part_v[i], lse_part[i])
+                    first[i] = False
+                k_off += k_len
+            if tl is not None:
+                ev1 = torch.cuda.Event(enable_timing=True)
+                ev1.record()
+                tl.append(("block", ev0, ev1))
+            self._wait(reqs, cur.is_cuda)
+            if tl is not None:
+                ev2 = torch.cuda.Event(enable_timing=True)
+                ev2.record()
+                tl.append(("wait", ev1, ev2))
+        for i in range(len(segs)):
+            if first[i]:  # every key of every block was masked for these queries
+                o_acc_v[i].zero_()
         self.backend.finish(o_acc, out16)
         return out16
 
@@ -126,15 +271,20 @@ class RingAttention:
 class ContextParallelTransformer:
     """Runs a UserOptimizedTransformer with its sequence sharded over `group`.
 
-    forward(x_local, valid_local=None) takes this rank's [B, S_loc, D] fp32
-    slice (shard_bounds of the full length) and returns the matching slice of
-    the output. Same arithmetic as the single-GPU forward, with the attention
-    of every layer done by RingAttention."""
+    forward(x_local, valid_local=None, layout=None) takes this rank's
+    [B, S_loc, D] fp32 rows (its layout segments, concatenated) and returns
+    the matching rows of the output. layout: per-rank segment lists
+    (contiguous_layout / zigzag_layout) or contiguous shard_bounds; None =
+    contiguous shards of the gathered local lengths. Same arithmetic as the
+    single-GPU forward, with the attention of every layer done by
+    RingAttention."""
 
-    def __init__(self, model, group=None, backend=None):
+    def __init__(self, model, group=None, backend=None, deadline_s: Optional[float] = None):
         self.model = model
         self.group = group
-        self.ring = RingAttention(group, backend)
+        self.ring = RingAttention(group, backend, deadline_s)
+        self.deadline_s = deadline_s
+        self._bufs: Dict[Tuple, Tuple] = {}
 
     def _gather_lengths(self, s_loc: int, device) -> List[int]:
         t = torch.tensor([s_loc], dtype=torch.int64, device=device)
@@ -142,8 +292,45 @@ class ContextParallelTransformer:
         dist.all_gather(out, t, group=self.group)
         return [int(v.item()) for v in out]
 
+    def _gather_mask(self, valid_local, layout, b, dev):
+        lens = [local_length(s) for s in layout]
+        parts = [torch.zeros(b, n, dtype=torch.bool, device=dev) for n in lens]
+        dist.all_gather(parts, valid_local.contiguous(), group=self.group)
+        total = sum(lens)
+        full = torch.zeros(b, total, dtype=torch.bool, device=dev)
+        for segs, part in zip(layout, parts):
+            off = 0
+            for s, n in segs:
+                full[:, s:s + n] = part[:, off:off + n]
+                off += n
+        return full
+
+    def _buffers(self, b, s_loc, d, f, dev):
+        key = (b, s_loc, d, f, dev)
+        bufs = self._bufs.get(key)
+        if bufs is None:
+            self._bufs.clear()
+            bufs = self._bufs[key] = (torch.empty(b, s_loc, d, dtype=torch.float32, device=dev),
+                                      torch.empty(b, s_loc, d, dtype=torch.float16, device=dev),
+                                      torch.empty(b, s_loc, 3 * d, dtype=torch.float16, device=dev),
+                                      torch.empty(b, s_loc, d, dtype=torch.float16, device=dev),
+                                      torch.empty(b, s_loc, f, dtype=torch.float16, device=dev))
+        return bufs
+
+    def _await(self, dev) -> None:
+        """Host deadline on the forward's device work (CUDA tensors)."""
+        ev = torch.cuda.Event()
+        ev.record()
+        t_end = time.monotonic() + self.deadline_s
+        while not ev.query():
+            if time.monotonic() > t_end:
+                self.ring.abort()
+                raise RingTimeout(f"rank {self.ring.rank}: context-parallel forward not done within "
+                                  f"{self.deadline_s} s; communicators aborted")
+            time.sleep(0.0002)
+
     def forward(self, x_local: torch.Tensor, valid_local: Optional[torch.Tensor] = None,
-                bounds: Optional[Sequence[Tuple[int, int]]] = None) -> torch.Tensor:
+                layout=None, bounds=None) -> torch.Tensor:
         m = self.model
         cfg = m.config
         if not x_local.is_cuda:
@@ -152,36 +339,33 @@ class ContextParallelTransformer:
             raise NotImplementedError("context parallelism runs the fp32 model (fp32 ring merge)")
         x_local = x_local.contiguous()
         b, s_loc, d = x_local.shape
-        if bounds is None:
+        if layout is None:
+            layout = bounds
+        if layout is None:
             lens = self._gather_lengths(s_loc, x_local.device)
             starts = [sum(lens[:i]) for i in range(len(lens))]
-            bounds = list(zip(starts, lens))
+            layout = list(zip(starts, lens))
+        layout = as_layout(layout)
+        dev = x_local.device
         mask_full = None
         vflat = None
         if valid_local is not None:
-            parts = [torch.zeros(b, length, dtype=torch.bool, device=x_local.device) for _, length in bounds]
-            dist.all_gather(parts, valid_local.contiguous(), group=self.group)
-            mask_full = torch.cat(parts, dim=1)
+            mask_full = self._gather_mask(valid_local, layout, b, dev)
             if bool(mask_full.all()):
                 mask_full = None
             else:
-                vflat = valid_local.reshape(-1)
+                vflat = valid_local.reshape(-1).contiguous()
         active = mask_full is not None
         h = cfg.num_heads
         scale = (d // h) ** -0.5
         wts = m._layer_weights()
-        dev = x_local.device
-        x_res = torch.empty(b, s_loc, d, dtype=torch.float32, device=dev)
-        normed = torch.empty(b, s_loc, d, dtype=torch.float16, device=dev)
-        qkv = torch.empty(b, s_loc, 3 * d, dtype=torch.float16, device=dev)
-        ctx = torch.empty(b, s_loc, d, dtype=torch.float16, device=dev)
-        hidden = torch.empty(b, s_loc, cfg.ffn_dim, dtype=torch.float16, device=dev)
+        x_res, normed, qkv, ctx, hidden = self._buffers(b, s_loc, d, cfg.ffn_dim, dev)
         cur = x_local
         for li, blk in enumerate(m.layers):
             w = wts[li]
             kernels.ln_residual(cur, None, w.n1w, w.n1b, blk.norm1.eps, normed=normed)
             kernels.linear(normed, w.wqkv, w.bqkv, out=qkv)
-            self.ring(qkv[..., :d], qkv[..., d:2 * d], qkv[..., 2 * d:], h, scale, cfg.causal, bounds, ctx,
+            self.ring(qkv[..., :d], qkv[..., d:2 * d], qkv[..., 2 * d:], h, scale, cfg.causal, layout, ctx,
                       mask_full)
             cur = kernels.linear_residual(ctx, w.wo, w.bo, cur, x_res, vflat, mask_delta=active)
             kernels.ln_residual(cur, None, w.n2w, w.n2b, blk.norm2.eps, normed=normed)
@@ -190,4 +374,6 @@ class ContextParallelTransformer:
         fn = m.final_norm
         _, out = kernels.ln_residual(cur, None, fn.weight, fn.bias, fn.eps, vflat, mask_out=active,
                                      out_dtype=torch.float32)
+        if self.deadline_s is not None:
+            self._await(dev)
         return out

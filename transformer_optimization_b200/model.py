@@ -144,17 +144,48 @@ def _splitk(m: int, n: int, k: int, sms: int) -> Optional[int]:
     return 0 if k >= 512 and tiles * 4 < sms else None
 
 
+# FFN row chunking (torch_transformer_benchmark.py:3841-3938): when the
+# [rows, ffn_dim] hidden activation would take more than this fraction of the
+# device's TOTAL memory (a hardware constant, so the decision is a pure
+# function of shape and card, and needs no device sync inside a captured
+# graph), FFN-in and FFN-out run over row chunks that reuse one hidden
+# buffer. Each row of this build's GEMMs is computed independently with the
+# same K order whatever the row count, so a chunked FFN is bit-identical to
+# the unchunked one. On a 180 GB B200 the budget is ~34 GB; BASELINE's
+# largest hidden (c4) is 2.1 GB, so c1-c5 never chunk.
+FFN_CHUNK_BUDGET_FRAC = 3.0 / 16.0
+FFN_CHUNK_MIN_ROWS = 256
+
+
+def ffn_chunk_rows(rows: int, ffn_dim: int, elem_bytes: int, budget_bytes: int) -> Optional[int]:
+    """Rows per FFN chunk, or None when the whole [rows, ffn_dim] hidden of
+    `elem_bytes`-byte elements fits `budget_bytes`. Otherwise the largest
+    power of two of rows whose hidden fits, but at least FFN_CHUNK_MIN_ROWS
+    (the reference's floor, below which per-chunk launches dominate) and at
+    most `rows` (torch_transformer_benchmark.py:3886-3908)."""
+    if rows <= 0 or rows * ffn_dim * elem_bytes <= budget_bytes:
+        return None
+    fit = budget_bytes // max(ffn_dim * elem_bytes, 1)
+    chunk = max(int(fit), FFN_CHUNK_MIN_ROWS)
+    chunk = 1 << (chunk.bit_length() - 1)
+    return min(chunk, rows)
+
+
 class _GraphCacheEntry:
     """One captured forward: static input/mask, the graph and its output
-    (torch_transformer_benchmark.py:2045-2068)."""
+    (torch_transformer_benchmark.py:2045-2068). `workspace` is the split-K
+    workspace the graph's kernels were captured with (or None): the entry
+    holds a reference so the caching allocator can never hand that memory to
+    another tensor while the graph may still replay into it."""
 
-    __slots__ = ("graph", "static_x", "static_mask", "static_output")
+    __slots__ = ("graph", "static_x", "static_mask", "static_output", "workspace")
 
-    def __init__(self, graph, static_x, static_mask, static_output) -> None:
+    def __init__(self, graph, static_x, static_mask, static_output, workspace=None) -> None:
         self.graph = graph
         self.static_x = static_x
         self.static_mask = static_mask
         self.static_output = static_output
+        self.workspace = workspace
 
 
 # Captured graphs keep their working set alive in a private pool; above this
@@ -180,11 +211,15 @@ class UserOptimizedTransformer(BaselineTransformer):
         self._graph_pool = None
         self._mask_all_true_cache: Dict[Tuple, bool] = {}
         self._splitk_ws: Optional[torch.Tensor] = None  # fp32 partials of split-K projections
+        self._last_ws_used = False  # whether the last _forward_core used _splitk_ws
         self.use_cuda_graphs = True
         # FFN-out with split (hi/lo fp16) weights: twice that GEMM's tensor
         # work for a near-fp32 weight. None = automatic (deep stacks only,
         # where fp16 weight rounding accumulates over many residual adds).
         self.precise_ffn_out: Optional[bool] = None
+        # bytes of hidden activation above which the FFN runs in row chunks;
+        # None = FFN_CHUNK_BUDGET_FRAC of the device's total memory
+        self.ffn_chunk_budget_bytes: Optional[int] = None
 
     def _model_dtype(self) -> torch.dtype:
         return self.final_norm.weight.dtype
@@ -250,16 +285,23 @@ class UserOptimizedTransformer(BaselineTransformer):
         half = x.dtype != torch.float32
         ct = wts[0].wqkv.dtype  # compute (operand) type
 
+        m, f = b * s, cfg.ffn_dim
+        props = torch.cuda.get_device_properties(dev)
+        budget = self.ffn_chunk_budget_bytes
+        if budget is None:
+            budget = int(props.total_memory * FFN_CHUNK_BUDGET_FRAC)
+        chunk = ffn_chunk_rows(m, f, torch.finfo(ct).bits // 8, budget)
+
         x_res = torch.empty(b, s, d, dtype=x.dtype, device=dev)
         normed = torch.empty(b, s, d, dtype=ct, device=dev)
         qkv = torch.empty(b, s, 3 * d, dtype=ct, device=dev)
         ctx = torch.empty(b, s, d, dtype=ct, device=dev)
-        hidden = torch.empty(b, s, cfg.ffn_dim, dtype=ct, device=dev)
+        hidden = torch.empty(b, s, f, dtype=ct, device=dev) if chunk is None else \
+            torch.empty(chunk, f, dtype=ct, device=dev)
 
         # split-K (fp32 partials in a workspace) for the projections of
         # few-row inputs, where 128-row tiles would leave most SMs idle
-        m, f = b * s, cfg.ffn_dim
-        sms = torch.cuda.get_device_properties(dev).multi_processor_count
+        sms = props.multi_processor_count
         sk_qkv, sk_o, sk_1 = _splitk(m, 3 * d, d, sms), _splitk(m, d, d, sms), _splitk(m, f, d, sms)
         sk_2 = None if wts[0].split_w2 else _splitk(m, d, f, sms)
         ws = None
@@ -268,7 +310,10 @@ class UserOptimizedTransformer(BaselineTransformer):
                        for n, k, v in ((3 * d, d, sk_qkv), (d, d, sk_o), (f, d, sk_1), (d, f, sk_2)) if v is not None)
             ws = self._splitk_ws
             if ws is None or ws.device != dev or ws.numel() < need:
+                # a new tensor; graphs captured with the old one hold it alive
+                # through their cache entries (_GraphCacheEntry.workspace)
                 ws = self._splitk_ws = torch.empty(need, dtype=torch.uint8, device=dev)
+        self._last_ws_used = ws is not None
 
         # With split-K residual projections (few rows), their reduce kernel also
         # runs the LayerNorm that follows (the next layer's norm1, or the final
@@ -291,6 +336,18 @@ class UserOptimizedTransformer(BaselineTransformer):
             else:
                 cur = kernels.linear_residual(ctx, w.wo, w.bo, cur, x_res, vflat, mask_delta=mask_active)
                 kernels.ln_residual(cur, None, w.n2w, w.n2b, blk.norm2.eps, normed=normed)
+            if chunk is not None:
+                # row-chunked FFN (cur is x_res here, updated in place)
+                n2, c2 = normed.view(m, d), cur.view(m, d)
+                for r0 in range(0, m, chunk):
+                    r1 = min(m, r0 + chunk)
+                    hc = hidden[:r1 - r0]
+                    kernels.linear(n2[r0:r1], w.w1, w.b1, gelu=True, out=hc, round_gelu_input=half)
+                    kernels.linear_residual(hc, w.w2, w.b2, c2[r0:r1], c2[r0:r1],
+                                            vflat[r0:r1] if vflat is not None else None, mask_x=mask_active,
+                                            w_split=w.split_w2)
+                normed_ready = False
+                continue
             kernels.linear(normed, w.w1, w.b1, gelu=True, out=hidden, splits=sk_1, workspace=ws,
                            round_gelu_input=half)
             if sk_2 is None:
@@ -338,7 +395,11 @@ class UserOptimizedTransformer(BaselineTransformer):
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph, pool=self._graph_pool):
             static_out = self._forward_core(static_x, static_mask, mask_active)
-        return _GraphCacheEntry(graph, static_x, static_mask, static_out)
+        # the workspace the captured kernels write (None when no projection of
+        # this shape is split): a later, larger shape replaces
+        # self._splitk_ws, and this reference keeps the old one alive
+        ws = self._splitk_ws if self._last_ws_used else None
+        return _GraphCacheEntry(graph, static_x, static_mask, static_out, ws)
 
     # ------------------------------------------------------------------ forward
     def forward(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
@@ -364,7 +425,8 @@ class UserOptimizedTransformer(BaselineTransformer):
 
         if not self.use_cuda_graphs or not self._graph_memory_safe(x):
             return self._forward_core(x, valid_token_mask, mask_active)
-        key = (tuple(x.shape), x.dtype, x.device, cfg.causal, mask_kind, self._split_ffn_out())
+        key = (tuple(x.shape), x.dtype, x.device, cfg.causal, mask_kind, self._split_ffn_out(),
+               self.ffn_chunk_budget_bytes)
         if key in self._graph_unsupported:
             return self._forward_core(x, valid_token_mask, mask_active)
         self._layer_weights()  # may invalidate cached graphs

@@ -2,12 +2,16 @@
 
     python -m transformer_optimization_b200.ncu_summary launches LAUNCHES.csv
         per kernel: launches, total device time, share (from an
-        `ncu --metrics gpu__time_duration.sum --csv --log-file` capture)
+        `ncu --metrics gpu__time_duration.sum --clock-control none --csv
+        --log-file` capture)
     python -m transformer_optimization_b200.ncu_summary report REPORT.ncu-rep
-        the figures the roofline needs from a `--set full` capture:
+        the figures the roofline needs from a `--set full --clock-control
+        none` capture:
         duration, DRAM bytes and throughput, tensor-pipe activity, warp
         stall reasons, registers (reads the report with `ncu -i --page raw`)
 
+Every capture is taken with `--clock-control none`: without it ncu locks
+the GPU's clocks, and a capture that is interrupted can leave them locked.
 Counters only; nothing here reads instruction-level output.
 """
 
