@@ -714,6 +714,9 @@ def main():
 
     if world > 1:
         import torch.distributed as dist
+        # NCCL's own messages (e.g. its version line) go to stderr, so that
+        # stdout carries only the JSON line
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))

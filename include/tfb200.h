@@ -79,6 +79,10 @@ extern "C" {
                                fp16 operands only */
 #define TF_ATTN_BF16 8      /* q, k, v and out (unless TF_ATTN_OUT_F32) are bf16;
                                P is rounded to bf16 for the PV product */
+#define TF_ATTN_ROUND_SCORES 16 /* the scores of the eager model run in the operand
+                               type T: T(T(q . k) * scale), then the fp32 softmax
+                               (half-precision models; default: fp32 scores);
+                               not with TF_ATTN_EXP_F16X2 or FMA-pipe exponentials */
 /* flags bits 8..15: how many of the 64 probability pairs per row and key
  * block are exponentiated on the FMA pipes instead of the exp unit
  * (0, 8, 16 or 24; with TF_ATTN_EXP_F16X2: 0 or 16; fp16 operands only) */
@@ -95,6 +99,20 @@ const char* tf_last_error(void);
  * No reference counterpart: the reference's Triton wrappers raise
  * (torch_transformer_benchmark.py:1053-1058) and cannot time out. */
 int tf_device_status(int* code, void* stream);
+
+/* Test hook for the bounded waits every pipeline kernel uses: launches one
+ * CTA that starts a 4 KiB bulk copy from `src` (16-byte aligned device
+ * memory of at least 4096 bytes) into shared memory, then waits on an
+ * mbarrier that nothing completes. That wait runs out after `limit_ns`
+ * (1000 .. 2e9) and records device code 106 in the status word; the thread
+ * then waits for its own copy (the drain every kernel does before it
+ * leaves) and returns. out: int32[3] device memory; out[0] = 1 when the wait
+ * ran out, out[1] = 1 when the copy drained, out[2] = the last byte copied.
+ * Afterwards tf_device_status returns TF_ERR_TIMEOUT with code 106 and sets
+ * tf_last_error; the device stays usable. No reference counterpart: the
+ * reference's kernels cannot time out; its guard is a host-side kill switch
+ * around the fast path (torch_transformer_benchmark.py:2368-2403). */
+int tf_test_wait_timeout(const void* src, int64_t limit_ns, int* out, void* stream);
 
 /* One residual-add + LayerNorm site over a contiguous [M, D] activation:
  *   x_new  = mask_x(x + mask_delta(fp32(delta)))

@@ -426,3 +426,27 @@ def attention_fp16(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: flo
     p = torch.exp(s - lse[..., None])
     p = torch.nan_to_num(p, nan=0.0)
     return torch.matmul(p, v.float()), lse
+
+
+def attention_rounded_scores(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float,
+                             causal: bool, key_valid: Optional[torch.Tensor] = None,
+                             q_offset: int = 0) -> Tuple[torch.Tensor, torch.Tensor]:
+    """attention_fp16 on T-valued q/k/v [B,H,S,hd] (T = q.dtype, fp16 or
+    bf16) with the scores the eager model computes in T:
+    T(T(q k^T) * scale) - the product accumulated in fp32 and rounded once
+    to T, then the scale applied in fp32 and rounded to T
+    (torch_transformer_benchmark.py:173) - then the fp32 softmax (:188) and
+    an fp32 P V. Returns (out fp32, lse of the rounded scores)."""
+    dt = q.dtype
+    s = torch.matmul(q.float(), k.float().transpose(-2, -1)).to(dt)
+    s = (s.float() * float(scale)).to(dt).float()
+    sq, sk = q.shape[-2], k.shape[-2]
+    if causal:
+        qi = torch.arange(sq)[:, None] + q_offset
+        kj = torch.arange(sk)[None, :]
+        s = s.masked_fill((kj > qi).to(s.device), float("-inf"))
+    if key_valid is not None:
+        s = s.masked_fill(~key_valid[:, None, None, :].to(s.device), float("-inf"))
+    lse = torch.logsumexp(s, dim=-1)
+    p = torch.nan_to_num(torch.exp(s - lse[..., None]), nan=0.0)
+    return torch.matmul(p, v.float()), lse

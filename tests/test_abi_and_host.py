@@ -57,7 +57,7 @@ def test_header_symbols_exported(lib):
 
 
 def test_abi_version_and_error_string(lib):
-    assert lib.tf_abi_version() == 9
+    assert lib.tf_abi_version() == 10
     assert isinstance(lib.tf_last_error(), bytes)
 
 

@@ -202,6 +202,49 @@ def test_flash_bf16(K, b, h, sq, sk, hd, causal, masked):
     assert torch.allclose(lse.cpu(), lse_ref, atol=5e-3, rtol=1e-3)
 
 
+@pytest.mark.parametrize("dt", [torch.float16, torch.bfloat16], ids=_name)
+@pytest.mark.parametrize("b,h,sq,sk,hd,causal,masked", [
+    (2, 4, 256, 256, 64, False, False),
+    (1, 2, 300, 300, 64, True, False),
+    (2, 2, 200, 333, 128, False, True),
+    (1, 4, 1024, 1024, 128, True, False),
+])
+def test_flash_round_scores(K, dt, b, h, sq, sk, hd, causal, masked):
+    """TF_ATTN_ROUND_SCORES: the scores of the eager model in T,
+    T(T(q . k) * scale), before the fp32 softmax (oracle
+    attention_rounded_scores). Inputs scaled by 3 so that the score
+    rounding is coarse. P is rounded to T for the PV product:
+    |d| <= 2 ulp(T)*|ref| + 2e-3; the LSE is that of the rounded scores."""
+    g = torch.Generator().manual_seed(b * 5 + sq + sk + hd + (1 if dt == torch.bfloat16 else 0))
+    d = h * hd
+    q = (torch.randn(b, sq, d, generator=g) * 3).to(dt)
+    kk = (torch.randn(b, sk, d, generator=g) * 3).to(dt)
+    vv = torch.randn(b, sk, d, generator=g).to(dt)
+    kv = None
+    if masked:
+        kv = torch.rand(b, sk, generator=g) > 0.3
+        kv[:, 0] = True
+    scale = hd ** -0.5
+
+    def heads(t):
+        return t.view(t.shape[0], t.shape[1], h, hd).transpose(1, 2)
+
+    ref, lse_ref = om.attention_rounded_scores(heads(q), heads(kk), heads(vv), scale, causal, kv)
+    ref = ref.transpose(1, 2).reshape(b, sq, d)
+    dv = torch.device("cuda:0")
+    out, lse = K.flash_attention(q.to(dv), kk.to(dv), vv.to(dv), h, scale, causal=causal,
+                                 key_valid=None if kv is None else kv.to(dv), want_lse=True, round_scores=True)
+    torch.cuda.synchronize()
+    assert out.dtype == dt
+    ulp = 2.0 ** -7 if dt == torch.bfloat16 else 2.0 ** -10
+    _assert_within(out, ref, 2 * ulp * ref.abs() + 2e-3, "attention (rounded scores)")
+    assert torch.allclose(lse.cpu(), lse_ref, atol=2e-3, rtol=1e-4)
+    # the fp32-score kernel on the same input lands further from these scores
+    out32, lse32 = K.flash_attention(q.to(dv), kk.to(dv), vv.to(dv), h, scale, causal=causal,
+                                     key_valid=None if kv is None else kv.to(dv), want_lse=True)
+    assert (lse32.cpu() - lse_ref).abs().mean() >= (lse.cpu() - lse_ref).abs().mean()
+
+
 def test_half_flag_errors(K):
     """Operand types that do not pair are refused, not converted."""
     dv = torch.device("cuda:0")

@@ -29,7 +29,10 @@ FAKE_RUN_BENCH = textwrap.dedent("""
     from pathlib import Path
     SCRIPT = Path(__file__).parent / "torch_transformer_benchmark.py"
     PEAK_TFLOPS = {"float32": 24.7, "float16": 48.8, "bfloat16": 49.4}
+    SUITES = {"quick": {"default_fp32": []}}
     def main():
+        print("suites", ",".join(sorted(SUITES)))
+        print("c3args", " ".join(SUITES.get("b200_baseline", {}).get("c3", [])))
         out = subprocess.run([sys.executable, str(SCRIPT), "--batch-size", "2"], capture_output=True, text=True)
         print("script", SCRIPT)
         print("peak16", PEAK_TFLOPS["float16"])
@@ -64,6 +67,10 @@ def test_run_bench_uses_this_script_and_b200_peaks(tmp_path):
     assert f"peak16 {rh.b200_peak_tflops()['float16']}" in r.stdout
     assert f"class {Ours.__module__} UserOptimizedTransformer" in r.stdout  # the per-case run went through us
     assert "optimized: median=1.25 ms" in r.stdout
+    # BASELINE's c1-c3 shapes are offered as the driver's "b200_baseline" suite
+    assert "suites b200_baseline,quick" in r.stdout
+    assert ("c3args --batch-size 8 --seq-len 2048 --d-model 1024 --heads 16 --ffn-dim 4096 --layers 12"
+            in r.stdout)
 
 
 def test_b200_peaks(tmp_path):

@@ -49,6 +49,7 @@ TF_ATTN_CAUSAL = 1
 TF_ATTN_OUT_F32 = 2
 TF_ATTN_EXP_F16X2 = 4
 TF_ATTN_BF16 = 8
+TF_ATTN_ROUND_SCORES = 16
 
 # every symbol include/tfb200.h declares, with its ctypes signature
 _P = ctypes.c_void_p
@@ -59,6 +60,7 @@ SIGNATURES = {
     "tf_abi_version": ([], _I),
     "tf_last_error": ([], ctypes.c_char_p),
     "tf_device_status": ([ctypes.POINTER(_I), _P], _I),
+    "tf_test_wait_timeout": ([_P, _I64, _P, _P], _I),
     "tf_ln_residual": ([_P, _P, _P, _P, _F, _P, _I64, _I64, _I, _P, _P, _P], _I),
     "tf_gemm": ([_P, _I64, _P, _I64, _P, _P, _I64, _I64, _I64, _I64, _I, _P], _I),
     "tf_gemm_tiled": ([_P, _I64, _P, _I64, _P, _P, _I64, _I64, _I64, _I64, _I, _I, _I, _P], _I),

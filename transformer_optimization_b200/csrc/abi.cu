@@ -166,7 +166,7 @@ static inline int begin_call() {
 
 extern "C" {
 
-int tf_abi_version(void) { return 9; }
+int tf_abi_version(void) { return 10; }
 
 const char* tf_last_error(void) { return tfb::g_msg; }
 
@@ -184,6 +184,12 @@ int tf_device_status(int* code, void* stream) {
   if (e != cudaSuccess) return set_error(TF_ERR_DEVICE, "clear status: %s", cudaGetErrorString(e));
   *code = host;
   return host == 0 ? TF_OK : set_error(TF_ERR_TIMEOUT, "a kernel wait ran out (device code %d)", host);
+}
+
+int tf_test_wait_timeout(const void* src, int64_t limit_ns, int* out, void* stream) {
+  int rc = begin_call();
+  if (rc) return rc;
+  return tfb::wait_timeout_probe(src, limit_ns, out, as_stream(stream));
 }
 
 int tf_ln_residual(const void* x, const void* delta, const float* w, const float* b, float eps,

@@ -31,6 +31,7 @@ enum DeviceError : int {
   kDevTimeoutEpilogue = 103,
   kDevTimeoutSoftmax = 104,
   kDevTimeoutDrain = 105,
+  kDevTimeoutProbe = 106,  // tf_test_wait_timeout: the wait made to run out
 };
 
 // Wall-time bound of a single wait: far above any legitimate wait (the
@@ -96,7 +97,8 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // completes is seen at once instead of behind a memory round trip.
 constexpr long long kSlowCheckCycles = 1ll << 20;  // ~0.5 ms
 
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code) {
+__device__ __forceinline__ bool mbar_wait_ns(uint64_t* bar, uint32_t parity, int* status, int code,
+                                             uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   long long next_check = clock64() + kSlowCheckCycles;
   uint64_t t0 = 0;
@@ -109,12 +111,16 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* s
       const uint64_t g = globaltimer_ns();
       if (t0 == 0) {
         t0 = g;
-      } else if (g - t0 > kWaitLimitNs) {
+      } else if (g - t0 > limit_ns) {
         record_error(status, code);
         return false;
       }
     }
   }
+}
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code) {
+  return mbar_wait_ns(bar, parity, status, code, kWaitLimitNs);
 }
 
 // ---------------------------------------------------------------------------

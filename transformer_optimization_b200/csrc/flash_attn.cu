@@ -64,7 +64,8 @@ struct AttnKParams {
   const uint8_t* key_valid;
   int heads, seq_q, seq_k;
   int q_blocks;      // CTAs along the query axis (256 rows each)
-  float scale_log2;  // scale * log2(e)
+  float scale_log2;  // scale * log2(e); log2(e) with RND (the scores arrive scaled)
+  float scale;       // the softmax scale, applied in the score type with RND
   long long q_pos0, k_pos0;
   int flags;
   int* status;
@@ -222,7 +223,11 @@ __device__ __forceinline__ void rescale_o(uint32_t taddr, float alpha) {
   tmem_wait_st();
 }
 
-template <int HD, bool EXP16, int POLY, int DT>
+// RND (TF_ATTN_ROUND_SCORES, half-precision models): the scores are those of
+// the eager model run in the operand type T, T(T(q . k) * scale)
+// (torch_transformer_benchmark.py:173: matmul in T, then the scale in T),
+// before the fp32 softmax (:188); without it the scores stay fp32.
+template <int HD, bool EXP16, int POLY, int DT, bool RND = false>
 __global__ void __launch_bounds__(kAttnThreads, 1)
     flash_fwd_tcgen05(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                       const __grid_constant__ CUtensorMap tmV, AttnKParams p) {
@@ -453,6 +458,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 #pragma unroll
         for (int i = 0; i < 128; ++i) s[i] = __uint_as_float(v[i]);
       }
+      if constexpr (RND) {
+#pragma unroll
+        for (int i = 0; i < 128; i += 2) {
+          const float2 qk = unpack2<DT>(pack2<DT>(s[i], s[i + 1]));                   // T(q . k)
+          const float2 sc = unpack2<DT>(pack2<DT>(qk.x * p.scale, qk.y * p.scale));  // T(T(q . k) * scale)
+          s[i] = sc.x;
+          s[i + 1] = sc.y;
+        }
+      }
 
       // ---- masking (tails, causal diagonal, key padding) ----
       const long long kbase = static_cast<long long>(j) * kAttnBN;
@@ -670,11 +684,11 @@ __global__ void attn_merge_kernel(float* __restrict__ o_acc, float* __restrict__
 // host side
 // ---------------------------------------------------------------------------
 
-template <int HD, bool EXP16, int POLY, int DT = kDtF16>
+template <int HD, bool EXP16, int POLY, int DT = kDtF16, bool RND = false>
 static int launch_flash(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                         const AttnKParams& kp, dim3 grid, cudaStream_t stream) {
   using C = AttnCfg<HD>;
-  auto kern = flash_fwd_tcgen05<HD, EXP16, POLY, DT>;
+  auto kern = flash_fwd_tcgen05<HD, EXP16, POLY, DT, RND>;
   static bool attr_done[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -734,7 +748,9 @@ int flash_fwd(const AttnArgs& a, cudaStream_t stream) {
   kp.seq_q = static_cast<int>(a.seq_q);
   kp.seq_k = static_cast<int>(a.seq_k);
   kp.q_blocks = static_cast<int>((a.seq_q + kAttnBM * kAttnTiles - 1) / (kAttnBM * kAttnTiles));
-  kp.scale_log2 = a.scale * 1.4426950408889634f;
+  const bool rnd = (a.flags & TF_ATTN_ROUND_SCORES) != 0;
+  kp.scale = a.scale;
+  kp.scale_log2 = rnd ? 1.4426950408889634f : a.scale * 1.4426950408889634f;
   kp.q_pos0 = a.q_pos0;
   kp.k_pos0 = a.k_pos0;
   kp.flags = a.flags;
@@ -749,14 +765,22 @@ int flash_fwd(const AttnArgs& a, cudaStream_t stream) {
     return set_error(TF_ERR_SHAPE, "flash: FMA-pipe exp pairs must be 0, 8, 16 or 24");
   if (exp16 && poly != 0 && poly != 16)
     return set_error(TF_ERR_SHAPE, "flash: with TF_ATTN_EXP_F16X2 the FMA-pipe exp pairs must be 0 or 16");
+  if (rnd && (exp16 || poly != 0))
+    return set_error(TF_ERR_SHAPE, "flash: TF_ATTN_ROUND_SCORES takes neither TF_ATTN_EXP_F16X2 nor FMA-pipe exponentials");
   if (a.flags & TF_ATTN_BF16) {
     // bf16 operands: fp32 exp2 on the exp unit only (the other exponential
     // forms produce fp16 bits)
     if (exp16 || poly != 0)
       return set_error(TF_ERR_SHAPE, "flash: TF_ATTN_BF16 takes neither TF_ATTN_EXP_F16X2 nor FMA-pipe exponentials");
+    if (rnd)
+      return a.head_dim == 64 ? launch_flash<64, false, 0, kDtBF16, true>(tq, tk, tv, kp, grid, stream)
+                              : launch_flash<128, false, 0, kDtBF16, true>(tq, tk, tv, kp, grid, stream);
     return a.head_dim == 64 ? launch_flash<64, false, 0, kDtBF16>(tq, tk, tv, kp, grid, stream)
                             : launch_flash<128, false, 0, kDtBF16>(tq, tk, tv, kp, grid, stream);
   }
+  if (rnd)
+    return a.head_dim == 64 ? launch_flash<64, false, 0, kDtF16, true>(tq, tk, tv, kp, grid, stream)
+                            : launch_flash<128, false, 0, kDtF16, true>(tq, tk, tv, kp, grid, stream);
 #define TFB_FLASH(E, P)                                                            \
   return a.head_dim == 64 ? launch_flash<64, E, P>(tq, tk, tv, kp, grid, stream) \
                           : launch_flash<128, E, P>(tq, tk, tv, kp, grid, stream);

@@ -142,4 +142,7 @@ struct MergeArgs {
 
 int attn_merge(const MergeArgs& a, cudaStream_t stream);
 
+// test probe of the bounded waits (probe.cu)
+int wait_timeout_probe(const void* src, long long limit_ns, int* out, cudaStream_t stream);
+
 }  // namespace tfb

@@ -272,14 +272,15 @@ def flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, heads: in
                     causal: bool = False, key_valid: Optional[torch.Tensor] = None, q_pos0: int = 0,
                     k_pos0: int = 0, out: Optional[torch.Tensor] = None, out_dtype: Optional[torch.dtype] = None,
                     lse: Optional[torch.Tensor] = None, want_lse: bool = False, exp_f16x2: bool = False,
-                    fma_exp_pairs: int = 0):
+                    fma_exp_pairs: int = 0, round_scores: bool = False):
     """Flash attention forward (tf_flash_fwd).
 
     q: [B, Sq, H*hd] fp16 or bf16 view with unit inner stride (may be a
     column slice of a packed QKV buffer), k, v: [B, Sk, H*hd] likewise, of
     q's type. Returns out [B, Sq, H*hd] (q's type unless out_dtype is fp32)
     and, with want_lse or an lse buffer, the natural-log sum-exp [B, H, Sq]
-    fp32."""
+    fp32. round_scores: the scores of the eager model in q's type,
+    T(T(q . k) * scale), before the fp32 softmax (half-precision models)."""
     _need_cuda("flash_attention", q, k, v, key_valid, out, lse)
     for t in (q, k, v):
         if t.dtype not in HALF_TYPES or t.dtype != q.dtype or t.dim() != 3 or t.stride(-1) != 1:
@@ -311,6 +312,8 @@ def flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, heads: in
         flags |= _abi.TF_ATTN_BF16
     if exp_f16x2:
         flags |= _abi.TF_ATTN_EXP_F16X2
+    if round_scores:
+        flags |= _abi.TF_ATTN_ROUND_SCORES
     flags |= (int(fma_exp_pairs) & 0xFF) << 8
     _abi.call("tf_flash_fwd", _ptr(q), _ptr(k), _ptr(v), q.stride(1), k.stride(1), q.stride(0), k.stride(0),
               _ptr(out), out.stride(1), out.stride(0), _ptr(lse), _ptr(key_valid), bsz, heads, sq, sk, hd,
@@ -335,3 +338,16 @@ def attn_merge(o_acc: torch.Tensor, lse_acc: torch.Tensor, o_part: torch.Tensor,
     bs16 = out16.stride(0) if out16 is not None else 0
     _abi.call("tf_attn_merge", _ptr(o_acc), _ptr(lse_acc), _ptr(o_part), _ptr(lse_part), o_acc.stride(1),
               o_acc.stride(0), _ptr(out16), ld16, bs16, bsz, heads, sq, dq // heads, _stream())
+
+
+def wait_timeout_probe(src: torch.Tensor, limit_ns: int) -> torch.Tensor:
+    """Run the bounded-wait probe (tf_test_wait_timeout): a wait that nothing
+    completes runs out after limit_ns and records device code 106; the probe
+    drains its own 4 KiB copy from `src` and returns. Returns the int32[3]
+    result (timed out, drained, last byte copied) on the device."""
+    _need_cuda("wait_timeout_probe", src)
+    if src.numel() * src.element_size() < 4096 or not src.is_contiguous():
+        raise ValueError("wait_timeout_probe: src must be contiguous with at least 4096 bytes")
+    out = torch.full((3,), -7, dtype=torch.int32, device=src.device)
+    _abi.call("tf_test_wait_timeout", _ptr(src), int(limit_ns), _ptr(out), _stream())
+    return out

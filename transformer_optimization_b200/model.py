@@ -151,7 +151,9 @@ def _splitk(m: int, n: int, k: int, sms: int) -> Optional[int]:
 # graph), FFN-in and FFN-out run over row chunks that reuse one hidden
 # buffer. Each row of this build's GEMMs is computed independently with the
 # same K order whatever the row count, so a chunked FFN is bit-identical to
-# the unchunked one. On a 180 GB B200 the budget is ~34 GB; BASELINE's
+# the unchunked one (the few-row split-K form, whose fixed-order sum of K
+# parts rounds differently, only serves inputs thousands of times below the
+# chunking threshold). On a 180 GB B200 the budget is ~34 GB; BASELINE's
 # largest hidden (c4) is 2.1 GB, so c1-c5 never chunk.
 FFN_CHUNK_BUDGET_FRAC = 3.0 / 16.0
 FFN_CHUNK_MIN_ROWS = 256
@@ -220,6 +222,11 @@ class UserOptimizedTransformer(BaselineTransformer):
         # bytes of hidden activation above which the FFN runs in row chunks;
         # None = FFN_CHUNK_BUDGET_FRAC of the device's total memory
         self.ffn_chunk_budget_bytes: Optional[int] = None
+        # half-precision models: attention scores rounded as the eager model
+        # in T rounds them, T(T(q . k) * scale) (torch_transformer_benchmark.py:
+        # 173); False keeps fp32 scores (closer to the fp32 model, further
+        # from eager T)
+        self.round_half_scores = True
 
     def _model_dtype(self) -> torch.dtype:
         return self.final_norm.weight.dtype
@@ -328,7 +335,8 @@ class UserOptimizedTransformer(BaselineTransformer):
                 kernels.ln_residual(cur, None, w.n1w, w.n1b, blk.norm1.eps, normed=normed)
             kernels.linear(normed, w.wqkv, w.bqkv, out=qkv, splits=sk_qkv, workspace=ws)
             kernels.flash_attention(qkv[..., :d], qkv[..., d:2 * d], qkv[..., 2 * d:], h, scale,
-                                    causal=cfg.causal, key_valid=kvalid, out=ctx)
+                                    causal=cfg.causal, key_valid=kvalid, out=ctx,
+                                    round_scores=half and self.round_half_scores)
             if sk_o is not None:
                 cur, _ = kernels.linear_residual_ln(ctx, w.wo, w.bo, cur, x_res, vflat, w.n2w, w.n2b,
                                                     blk.norm2.eps, mask_delta=mask_active, normed=normed,
@@ -426,7 +434,7 @@ class UserOptimizedTransformer(BaselineTransformer):
         if not self.use_cuda_graphs or not self._graph_memory_safe(x):
             return self._forward_core(x, valid_token_mask, mask_active)
         key = (tuple(x.shape), x.dtype, x.device, cfg.causal, mask_kind, self._split_ffn_out(),
-               self.ffn_chunk_budget_bytes)
+               self.ffn_chunk_budget_bytes, self.round_half_scores)
         if key in self._graph_unsupported:
             return self._forward_core(x, valid_token_mask, mask_active)
         self._layer_weights()  # may invalidate cached graphs

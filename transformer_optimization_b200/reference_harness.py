@@ -108,14 +108,33 @@ def run_reference_script(reference_dir: Path, argv: List[str]) -> int:
     return int(ref.main() or 0)
 
 
+# BASELINE's configs that the reference's eager fp32 model can run densely
+# on one B200 (c4 and c5 need its query-tiled / streamed protocols), as
+# run_bench case arguments in the reference's own flag vocabulary
+# (torch_transformer_benchmark.py:5028-5034); added to run_bench's suites as
+# "b200_baseline".
+B200_SUITE = {
+    "c1": ["--batch-size", "2", "--seq-len", "128", "--d-model", "256", "--heads", "4", "--ffn-dim", "1024",
+           "--layers", "2"],
+    "c2": ["--batch-size", "1", "--seq-len", "64", "--d-model", "512", "--heads", "8", "--ffn-dim", "2048",
+           "--layers", "6"],
+    "c3": ["--batch-size", "8", "--seq-len", "2048", "--d-model", "1024", "--heads", "16", "--ffn-dim", "4096",
+           "--layers", "12"],
+}
+
+
 def run_bench(reference_dir: Path, argv: List[str]) -> int:
     """The reference's suite driver with this file as its per-case script and
-    B200 peaks for its MFU."""
+    B200 peaks for its MFU, plus the "b200_baseline" suite (B200_SUITE).
+    run_bench writes its results JSON beside its per-case script, i.e. under
+    this package's agent/results/ (run_bench.py:527-530)."""
     reference_dir = Path(reference_dir).resolve()
     os.environ[ENV_REFERENCE_DIR] = str(reference_dir)
     rb = _load("run_bench", reference_dir / "run_bench.py")
     rb.SCRIPT = _HERE
     rb.PEAK_TFLOPS = b200_peak_tflops()
+    if hasattr(rb, "SUITES"):
+        rb.SUITES["b200_baseline"] = {k: list(v) for k, v in B200_SUITE.items()}
     sys.argv = [str(reference_dir / "run_bench.py"), *argv]
     return int(rb.main() or 0)
 
