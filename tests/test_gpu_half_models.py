@@ -7,8 +7,10 @@ input (TF32 off), which both T results approximate.
 
 Gates:
 * no less accurate than the eager model in T: against the fp32 model, mean
-  |error| <= 1.02x the eager model's (the robust statistic) and max |error|
-  <= 1.5x (one element each; they differ by up to ~20% either way between
+  |error| <= 1.02x the eager model's (the robust statistic), the 99.9th
+  percentile of |error| <= 1.5x the eager model's, and max |error| <= 2x (one
+  element each: with the eager model's score rounding the two worst elements
+  land on different tokens, and their ratio varies by tens of percent between
   trials).
 * against the eager model in T, the reference's gate (compare_outputs, zero
   failing elements) with both thresholds scaled for two independently rounded
@@ -80,7 +82,10 @@ def _check(out, eager, f32, dt):
     e_ours = (out - f32).abs()
     e_eager = (eager - f32).abs()
     assert float(e_ours.mean()) <= 1.02 * float(e_eager.mean()) + 1e-7, (float(e_ours.mean()), float(e_eager.mean()))
-    assert float(e_ours.max()) <= 1.5 * float(e_eager.max()) + 1e-6, (float(e_ours.max()), float(e_eager.max()))
+    q_ours = float(torch.quantile(e_ours.flatten()[:1 << 24], 0.999))
+    q_eager = float(torch.quantile(e_eager.flatten()[:1 << 24], 0.999))
+    assert q_ours <= 1.5 * q_eager + 1e-6, (q_ours, q_eager)
+    assert float(e_ours.max()) <= 2.0 * float(e_eager.max()) + 1e-6, (float(e_ours.max()), float(e_eager.max()))
 
 
 @pytest.mark.parametrize("dt", [torch.float16, torch.bfloat16], ids=_name)
