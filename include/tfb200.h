@@ -222,33 +222,6 @@ int tf_gemm_residual_ln_splitk(const void* A, int64_t lda, const void* W, int64_
 int tf_gemm_splitk_static(const void* A, int64_t lda, const void* W, int64_t ldw, const float* bias, void* C,
                           int64_t ldc, int64_t M, int64_t N, int64_t K, int epilogue, int splits, void* stream);
 
-/* The whole forward pass of a few-row fp32 model in ONE persistent launch
- * (one CTA per SM, cooperative launch, grid-wide barriers between phases):
- * norm1 -> QKV GEMM -> attention -> out_proj (split-K) -> residual + norm2 ->
- * FFN-in + GELU -> FFN-out (split-K) -> residual + next norm1 (or the final
- * LayerNorm) per layer, with the arithmetic of the multi-kernel entry points
- * (fp16 tensor-core operands, fp32 accumulation, residual stream and
- * statistics). For inputs of a few hundred tokens every op is microseconds of
- * work and a chain of ~7 launches per layer is bound by launch latency.
- * x, out: fp32 [batch*seq, d_model]. Limits: seq <= 128 (one attention
- * block), batch*seq <= 512, head_dim 64 (d_model = 64*heads), d_model a
- * multiple of 128 up to 1024, ffn a multiple of 64 up to 8192, layers <= 16;
- * no key-padding mask. params: host array of 12*layers + 2 device pointers,
- * per layer Wqkv (fp16 [3D, D], q|k|v rows), bqkv (fp32 [3D]), Wo (fp16
- * [D, D]), bo, W1 (fp16 [F, D]), b1, W2 (fp16 [D, F]), b2, norm1 w, b, norm2
- * w, b (fp32 [D]); then the final LayerNorm w, b. eps: host array of
- * 2*layers + 1 (norm1, norm2 per layer, then final). workspace: device
- * memory of tf_forward_small_workspace() bytes, 256-byte aligned, owned by
- * the caller (activations, split-K partials and the barrier words, which the
- * call resets on its stream); calls on one workspace must not overlap.
- * Replaces the reference's whole per-layer schedule for small shapes, which
- * it runs as CUDA-graph replay of its kernel sequence
- * (torch_transformer_benchmark.py:3613-3725, 4003-4326). */
-int64_t tf_forward_small_workspace(int64_t batch, int64_t seq, int64_t d_model, int64_t ffn);
-int tf_forward_small(const float* x, float* out, int64_t batch, int64_t seq, int64_t d_model, int64_t heads,
-                     int64_t ffn, int64_t layers, int causal, const void* const* params, const float* eps,
-                     void* workspace, int64_t workspace_bytes, void* stream);
-
 /* Flash attention forward (online softmax, no score matrix in HBM):
  *   out[b, i, h*hd:(h+1)*hd] = sum_j softmax_j(scale * q_i . k_j) v_j
  * q: fp16 (bf16 with TF_ATTN_BF16), token i of batch b, head h at

@@ -148,7 +148,7 @@ def test_bench_algorithmic_bytes():
     assert 140e6 < bench.C3_GEMM_DRAM_BYTES_PER_LAUNCH < expect  # measured DRAM bytes below algorithmic
 
 
-def _record_schedule(monkeypatch, cfg, m_rows, chunk_budget=None, persistent=False, batch=1):
+def _record_schedule(monkeypatch, cfg, m_rows, chunk_budget=None):
     """Run the model's per-layer schedule with the kernel wrappers replaced
     by recorders (no GPU): returns [(wrapper, kwargs)] in call order."""
     import types
@@ -171,11 +171,9 @@ def _record_schedule(monkeypatch, cfg, m_rows, chunk_budget=None, persistent=Fal
     monkeypatch.setattr(K, "linear_residual", rec("res", lambda a, w, b, x_in, x_out, *r, **kw: x_out))
     monkeypatch.setattr(K, "linear_residual_ln",
                         rec("res_ln", lambda a, w, b, x_in, x_out, *r, **kw: (x_out, torch.zeros(1))))
-    monkeypatch.setattr(K, "forward_small", rec("small", lambda x, *a, **kw: x))
     model = UserOptimizedTransformer(cfg)
     model.ffn_chunk_budget_bytes = chunk_budget
-    model.persistent_small = persistent
-    model._forward_core(torch.zeros(batch, m_rows // batch, cfg.d_model), None, False)
+    model._forward_core(torch.zeros(1, m_rows, cfg.d_model), None, False)
     return calls
 
 
@@ -189,23 +187,6 @@ def test_forward_schedule_few_rows(monkeypatch):
     assert names == ["ln"] + ["linear", "flash", "res_ln", "linear", "res_ln"] * cfg.num_layers
     assert all(kw.get("splits") == 0 for n, kw in calls if n in ("linear", "res_ln"))
     assert calls[-1][1]["out_dtype"] == torch.float32 and calls[-1][1]["mask_out"] is False
-
-
-def test_forward_schedule_persistent_small(monkeypatch):
-    """c1 and c2 (256 and 64 rows, fp32, no key mask) run as one persistent
-    launch; c3-sized rows and shapes outside the kernel's limits do not."""
-    from transformer_optimization_b200.model import small_forward_shape_ok
-    for name in ("c1", "c2"):
-        c = NAMED_CONFIGS[name]
-        calls = _record_schedule(monkeypatch, c, c.batch_size * c.seq_len, persistent=True, batch=c.batch_size)
-        assert [n for n, _ in calls] == ["small"]
-    c3 = NAMED_CONFIGS["c3"]
-    assert not small_forward_shape_ok(c3.batch_size, c3.seq_len, c3.d_model, c3.num_heads, c3.ffn_dim, c3.num_layers)
-    assert not small_forward_shape_ok(1, 200, 512, 8, 2048, 6)   # two attention blocks per sequence
-    assert not small_forward_shape_ok(1, 64, 256, 2, 1024, 2)    # head_dim 128
-    assert not small_forward_shape_ok(4, 128, 512, 8, 2048, 6)   # 512 rows: the multi-kernel path
-    assert not small_forward_shape_ok(1, 64, 512, 8, 2048, 17)   # too many layers
-    assert small_forward_shape_ok(2, 100, 256, 4, 512, 2)
 
 
 def test_forward_schedule_many_rows(monkeypatch):

@@ -56,42 +56,6 @@ def test_small_configs(name):
     _check(ref, out)
 
 
-PERSISTENT = {
-    "c1": NAMED_CONFIGS["c1"],
-    "c1_causal": TransformerConfig(2, 128, 256, 4, 1024, 2, True),
-    "c2": NAMED_CONFIGS["c2"],
-    "c2_causal": TransformerConfig(1, 64, 512, 8, 2048, 6, True),
-    "ragged": TransformerConfig(2, 100, 256, 4, 512, 2, False),
-    "ragged_causal": TransformerConfig(3, 77, 128, 2, 256, 3, True),
-    "d1024": TransformerConfig(1, 128, 1024, 16, 4096, 2, True),
-}
-
-
-@pytest.mark.parametrize("name", sorted(PERSISTENT))
-def test_persistent_small_forward(name):
-    """Few-row fp32 inputs run as one persistent launch (tf_forward_small):
-    the reference's gate against the oracle, replays bit-identical, and the
-    result within 2e-3 of the multi-kernel schedule (same arithmetic, other
-    split-K partitions and attention kernel)."""
-    cfg = PERSISTENT[name]
-    p, x, model = _build(cfg, seed=11)
-    xg = x.cuda()
-    assert model._small_path(xg, False)
-    with torch.inference_mode():
-        out = model(xg)   # captured in a CUDA graph, then replayed
-        out2 = model(xg)
-        model.use_cuda_graphs = False
-        eager = model(xg)
-        model.persistent_small = False
-        multi = model(xg)
-    torch.cuda.synchronize()
-    from transformer_optimization_b200 import _abi
-    assert _abi.device_status() == 0
-    assert torch.equal(out, out2) and torch.equal(out, eager)
-    _check(om.forward(p, cfg, x), out)
-    assert float((out - multi).abs().max()) < 2e-3
-
-
 @pytest.mark.parametrize("causal", [False, True])
 def test_partial_mask(causal):
     cfg = TransformerConfig(3, 200, 256, 4, 1024, 2, causal)
@@ -136,7 +100,6 @@ def test_graphs_keep_their_splitk_workspace():
     never into memory the allocator has since handed to another tensor."""
     cfg = NAMED_CONFIGS["c2"]
     p, _, model = _build(cfg)
-    model.persistent_small = False  # the multi-kernel schedule owns the split-K workspace
     g = torch.Generator().manual_seed(5)
     x_small = torch.randn(1, 32, cfg.d_model, generator=g).cuda()
     x_big = torch.randn(2, 64, cfg.d_model, generator=g).cuda()

@@ -61,8 +61,6 @@ SIGNATURES = {
     "tf_last_error": ([], ctypes.c_char_p),
     "tf_device_status": ([ctypes.POINTER(_I), _P], _I),
     "tf_test_wait_timeout": ([_P, _I64, _P, _P], _I),
-    "tf_forward_small_workspace": ([_I64, _I64, _I64, _I64], _I64),
-    "tf_forward_small": ([_P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I, _P, _P, _P, _I64, _P], _I),
     "tf_ln_residual": ([_P, _P, _P, _P, _F, _P, _I64, _I64, _I, _P, _P, _P], _I),
     "tf_gemm": ([_P, _I64, _P, _I64, _P, _P, _I64, _I64, _I64, _I64, _I, _P], _I),
     "tf_gemm_tiled": ([_P, _I64, _P, _I64, _P, _P, _I64, _I64, _I64, _I64, _I, _I, _I, _P], _I),

@@ -192,32 +192,6 @@ int tf_test_wait_timeout(const void* src, int64_t limit_ns, int* out, void* stre
   return tfb::wait_timeout_probe(src, limit_ns, out, as_stream(stream));
 }
 
-int64_t tf_forward_small_workspace(int64_t batch, int64_t seq, int64_t d_model, int64_t ffn) {
-  return tfb::forward_small_workspace_bytes(batch, seq, d_model, ffn);
-}
-
-int tf_forward_small(const float* x, float* out, int64_t batch, int64_t seq, int64_t d_model, int64_t heads,
-                     int64_t ffn, int64_t layers, int causal, const void* const* params, const float* eps,
-                     void* workspace, int64_t workspace_bytes, void* stream) {
-  int rc = begin_call();
-  if (rc) return rc;
-  tfb::SmallFwdArgs a;
-  a.x = x;
-  a.out = out;
-  a.batch = batch;
-  a.seq = seq;
-  a.d_model = d_model;
-  a.heads = heads;
-  a.ffn = ffn;
-  a.layers = layers;
-  a.causal = causal;
-  a.params = params;
-  a.eps = eps;
-  a.workspace = workspace;
-  a.workspace_bytes = workspace_bytes;
-  return tfb::forward_small(a, as_stream(stream));
-}
-
 int tf_ln_residual(const void* x, const void* delta, const float* w, const float* b, float eps,
                    const uint8_t* valid, int64_t M, int64_t D, int flags, void* x_out, void* normed,
                    void* stream) {

@@ -142,20 +142,6 @@ struct MergeArgs {
 
 int attn_merge(const MergeArgs& a, cudaStream_t stream);
 
-// whole forward of a few-row fp32 model in one persistent launch (small_forward.cu)
-struct SmallFwdArgs {
-  const float* x;
-  float* out;
-  long long batch, seq, d_model, heads, ffn, layers;
-  int causal;
-  const void* const* params;  // per layer 12 device pointers, then the final LayerNorm w, b
-  const float* eps;           // per layer norm1, norm2 eps, then the final eps
-  void* workspace;
-  long long workspace_bytes;
-};
-int forward_small(const SmallFwdArgs& a, cudaStream_t stream);
-long long forward_small_workspace_bytes(long long B, long long S, long long D, long long F);
-
 // test probe of the bounded waits (probe.cu)
 int wait_timeout_probe(const void* src, long long limit_ns, int* out, cudaStream_t stream);
 

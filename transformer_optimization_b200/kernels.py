@@ -8,8 +8,7 @@ tensor on the CPU, a wrong dtype or a missing library raises.
 
 from __future__ import annotations
 
-import ctypes
-from typing import Optional, Sequence, Tuple
+from typing import Optional, Tuple
 
 import torch
 
@@ -351,45 +350,4 @@ def wait_timeout_probe(src: torch.Tensor, limit_ns: int) -> torch.Tensor:
         raise ValueError("wait_timeout_probe: src must be contiguous with at least 4096 bytes")
     out = torch.full((3,), -7, dtype=torch.int32, device=src.device)
     _abi.call("tf_test_wait_timeout", _ptr(src), int(limit_ns), _ptr(out), _stream())
-    return out
-
-
-def forward_small_workspace_bytes(batch: int, seq: int, d_model: int, ffn: int) -> int:
-    """Workspace bytes of tf_forward_small for this shape."""
-    _abi.load()
-    return int(_abi.call_value("tf_forward_small_workspace", int(batch), int(seq), int(d_model), int(ffn)))
-
-
-def forward_small(x: torch.Tensor, params: Sequence[torch.Tensor], eps: Sequence[float], heads: int, ffn: int,
-                  causal: bool, out: Optional[torch.Tensor] = None,
-                  workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """The whole forward of a few-row fp32 model in one persistent launch
-    (tf_forward_small). x: fp32 [B, S, D] contiguous; params: per layer
-    [Wqkv, bqkv, Wo, bo, W1, b1, W2, b2, n1w, n1b, n2w, n2b] (fp16 weights,
-    fp32 vectors, all contiguous on x's device), then the final LayerNorm
-    weight and bias; eps: per layer (norm1, norm2), then the final eps.
-    Returns out fp32 [B, S, D]."""
-    _need_cuda("forward_small", x, out, workspace, *params)
-    if x.dtype != torch.float32 or x.dim() != 3 or not x.is_contiguous():
-        raise ValueError("forward_small: x must be contiguous fp32 [B, S, D]")
-    b, s, d = x.shape
-    n_layers = (len(params) - 2) // 12
-    if len(params) != 12 * n_layers + 2 or len(eps) != 2 * n_layers + 1 or n_layers < 1:
-        raise ValueError("forward_small: 12 tensors per layer plus the final LayerNorm's two, and 2L+1 eps")
-    for i, t in enumerate(params):
-        want = torch.float16 if (i < 12 * n_layers and i % 12 in (0, 2, 4, 6)) else torch.float32
-        if t.dtype != want or not t.is_contiguous():
-            raise ValueError(f"forward_small: parameter {i} must be contiguous {want}")
-    if out is None:
-        out = torch.empty_like(x)
-    need = forward_small_workspace_bytes(b, s, d, ffn)
-    if workspace is None:
-        workspace = torch.empty(need, dtype=torch.uint8, device=x.device)
-    if workspace.numel() * workspace.element_size() < need:
-        raise ValueError(f"forward_small: workspace of {need} bytes needed")
-    ptrs = (ctypes.c_void_p * len(params))(*[t.data_ptr() for t in params])
-    eps_arr = (ctypes.c_float * len(eps))(*[float(e) for e in eps])
-    _abi.call("tf_forward_small", _ptr(x), _ptr(out), b, s, d, int(heads), int(ffn), n_layers, 1 if causal else 0,
-              ctypes.cast(ptrs, ctypes.c_void_p), ctypes.cast(eps_arr, ctypes.c_void_p), _ptr(workspace),
-              workspace.numel() * workspace.element_size(), _stream())
     return out

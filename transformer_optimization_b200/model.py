@@ -173,22 +173,6 @@ def ffn_chunk_rows(rows: int, ffn_dim: int, elem_bytes: int, budget_bytes: int) 
     return min(chunk, rows)
 
 
-# Few-row inputs run the whole forward in one persistent launch
-# (tf_forward_small: phases separated by grid-wide barriers instead of ~7
-# dependent launches per layer). Limits of that kernel, plus this module's
-# choice of where it pays: up to 256 rows (BASELINE's c1 and c2).
-SMALL_FORWARD_MAX_ROWS = 256
-
-
-def small_forward_shape_ok(b: int, s: int, d: int, heads: int, ffn: int, layers: int) -> bool:
-    """Whether tf_forward_small takes this shape: one attention block per
-    sequence (S <= 128), head_dim 64, d_model a multiple of 128 up to 1024,
-    ffn a multiple of 64 up to 8192, 1..16 layers, at most
-    SMALL_FORWARD_MAX_ROWS rows."""
-    return (0 < s <= 128 and 0 < b * s <= SMALL_FORWARD_MAX_ROWS and d % 128 == 0 and 0 < d <= 1024
-            and heads > 0 and d == 64 * heads and ffn % 64 == 0 and 0 < ffn <= 8192 and 1 <= layers <= 16)
-
-
 class _GraphCacheEntry:
     """One captured forward: static input/mask, the graph and its output
     (torch_transformer_benchmark.py:2045-2068). `workspace` is the split-K
@@ -238,10 +222,6 @@ class UserOptimizedTransformer(BaselineTransformer):
         # bytes of hidden activation above which the FFN runs in row chunks;
         # None = FFN_CHUNK_BUDGET_FRAC of the device's total memory
         self.ffn_chunk_budget_bytes: Optional[int] = None
-        # few-row fp32 inputs without a key mask: the whole forward in one
-        # persistent launch (tf_forward_small); False keeps the multi-kernel
-        # schedule for every shape
-        self.persistent_small = True
         # half-precision models: attention scores rounded as the eager model
         # in T rounds them, T(T(q . k) * scale) (torch_transformer_benchmark.py:
         # 173); False keeps fp32 scores (closer to the fp32 model, further
@@ -311,8 +291,6 @@ class UserOptimizedTransformer(BaselineTransformer):
         dev = x.device
         half = x.dtype != torch.float32
         ct = wts[0].wqkv.dtype  # compute (operand) type
-        if self._small_path(x, mask_active):
-            return self._forward_small(x, wts)
 
         m, f = b * s, cfg.ffn_dim
         props = torch.cuda.get_device_properties(dev)
@@ -400,27 +378,6 @@ class UserOptimizedTransformer(BaselineTransformer):
                                          out_dtype=x.dtype)
         return out
 
-    def _small_path(self, x: torch.Tensor, mask_active: bool) -> bool:
-        """Whether this forward runs as one persistent launch: fp32 model,
-        no partial key mask, plain fp16 weights, a shape the kernel takes."""
-        if not self.persistent_small or mask_active or x.dtype != torch.float32 or self._split_ffn_out():
-            return False
-        cfg = self.config
-        b, s, d = x.shape
-        return small_forward_shape_ok(b, s, d, cfg.num_heads, cfg.ffn_dim, len(self.layers))
-
-    def _forward_small(self, x: torch.Tensor, wts: list) -> torch.Tensor:
-        """The per-layer schedule of _forward_core in one launch of the
-        persistent kernel (tf_forward_small), same arithmetic."""
-        params, eps = [], []
-        for blk, w in zip(self.layers, wts):
-            params += [w.wqkv, w.bqkv, w.wo, w.bo, w.w1, w.b1, w.w2, w.b2, w.n1w, w.n1b, w.n2w, w.n2b]
-            eps += [blk.norm1.eps, blk.norm2.eps]
-        fw, fb = self._final_ln
-        params += [fw, fb]
-        eps.append(self.final_norm.eps)
-        return kernels.forward_small(x, params, eps, self.config.num_heads, self.config.ffn_dim, self.config.causal)
-
     # ------------------------------------------------------------------ graphs
     def _graph_memory_safe(self, x: torch.Tensor) -> bool:
         b, s, d = x.shape
@@ -477,7 +434,7 @@ class UserOptimizedTransformer(BaselineTransformer):
         if not self.use_cuda_graphs or not self._graph_memory_safe(x):
             return self._forward_core(x, valid_token_mask, mask_active)
         key = (tuple(x.shape), x.dtype, x.device, cfg.causal, mask_kind, self._split_ffn_out(),
-               self.ffn_chunk_budget_bytes, self.round_half_scores, self.persistent_small)
+               self.ffn_chunk_budget_bytes, self.round_half_scores)
         if key in self._graph_unsupported:
             return self._forward_core(x, valid_token_mask, mask_active)
         self._layer_weights()  # may invalidate cached graphs
