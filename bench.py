@@ -61,6 +61,14 @@ from transformer_optimization_b200 import NAMED_CONFIGS, UserOptimizedTransforme
 from transformer_optimization_b200 import kernels as K  # noqa: E402
 
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+_JSON_OUT = None  # the process's original stdout; everything else goes to stderr
+
+
+def emit(line: dict) -> None:
+    """Print the one JSON line on the original stdout."""
+    out = _JSON_OUT if _JSON_OUT is not None else sys.stdout
+    out.write(json.dumps(line) + "\n")
+    out.flush()
 # DRAM bytes (read + write) per projection launch of the c3 forward at one
 # GPU (M = 16384 rows), mean of the four projections of a layer, from one ncu
 # capture of each shape (the capture summaries are kept with the profiles)
@@ -405,7 +413,7 @@ def run_reference(args, cfg, rank):
                          "kind": "port", "sample": sample, "extrapolated": False},
         "e2e": {"value": tok_s, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 # ---------------------------------------------------------------- our arm
@@ -663,7 +671,7 @@ def run_ours(args, cfg, rank, world, local_rank):
                                           f"{cfg.num_layers} layers), median of {len(times)}",
                                 "extrapolated": False}
     if rank == 0:
-        print(json.dumps(line), flush=True)
+        emit(line)
 
 
 def measure_sharded_weak(c: Ctx, cfg, steps, window):
@@ -699,6 +707,12 @@ def main():
     ap.add_argument("--model-dtype", default="float32", choices=sorted(MODEL_DTYPES),
                     help="parameter and input dtype of the model (the BASELINE configs are float32)")
     args = ap.parse_args()
+    # stdout carries exactly the JSON line: the libraries' own prints (NCCL's
+    # version banner, for one) are sent to stderr at the file-descriptor level
+    global _JSON_OUT
+    sys.stdout.flush()
+    _JSON_OUT = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
     if args.warmup < 3:
         args.warmup = 3
     cfg = NAMED_CONFIGS[args.config]
@@ -714,9 +728,6 @@ def main():
 
     if world > 1:
         import torch.distributed as dist
-        # NCCL's own messages (e.g. its version line) go to stderr, so that
-        # stdout carries only the JSON line
-        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
@@ -760,7 +771,7 @@ def run_cp_headline(args, cfg, rank, world, local_rank):
         "ring": r.get("ring"), "clocks": c.clk.summary(), "tokens": tokens,
     }
     if rank == 0:
-        print(json.dumps(line), flush=True)
+        emit(line)
 
 
 if __name__ == "__main__":
