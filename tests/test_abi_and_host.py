@@ -126,11 +126,12 @@ def test_mask_resolution_memoised(monkeypatch):
 
 def test_splitk_choice():
     """Few-row projections take the split-K form (fewer than a quarter of the
-    SMs would get a 128x64 tile, K >= 512); the c3-sized ones do not."""
+    SMs would get a 128x64 tile, K >= 256); the c3-sized ones do not."""
     from transformer_optimization_b200.model import _splitk
     assert _splitk(64, 512, 2048, 148) == 0      # c2 FFN-out
     assert _splitk(256, 256, 1024, 148) == 0     # c1 FFN-out
-    assert _splitk(256, 768, 256, 148) is None   # c1 QKV: K too short to split
+    assert _splitk(256, 768, 256, 148) == 0      # c1 QKV
+    assert _splitk(256, 768, 128, 148) is None   # K too short to split
     assert _splitk(16384, 3072, 1024, 148) is None
     assert _splitk(64, 512, 2048, 16) is None    # few SMs: enough tiles already
 
@@ -224,7 +225,8 @@ def test_forward_schedule_chunked_ffn(monkeypatch):
     cfg = TransformerConfig(1, 1000, 256, 4, 1024, 2, False)
     calls = _record_schedule(monkeypatch, cfg, 1000, chunk_budget=300 * 1024 * 2)
     names = [c[0] for c in calls]
-    assert names == (["ln", "linear", "flash", "res", "ln"] + ["linear", "res"] * 4) * cfg.num_layers + ["ln"]
+    # (1000 rows: the out-projection takes the split-K form, whose reduce runs norm2)
+    assert names == (["ln", "linear", "flash", "res_ln"] + ["linear", "res"] * 4) * cfg.num_layers + ["ln"]
 
 
 C_PROGRAM = r"""

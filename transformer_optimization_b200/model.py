@@ -137,11 +137,12 @@ class _LayerWeights:
 def _splitk(m: int, n: int, k: int, sms: int) -> Optional[int]:
     """0 (automatic split count) when a projection of m rows should use the
     split-K form, else None: fewer than a quarter of the SMs would get a
-    128 x 64 tile and K has at least 8 blocks of 64 to split (measured on
-    the c1/c2 shapes: the 64-row FFN-out drops from 13.5 to 6-7 us; K = 256
-    projections do not gain)."""
+    128 x 64 tile and K has at least 4 blocks of 64 to split (measured on
+    the c1/c2 shapes: the 64-row FFN-out drops from 13.5 to 6-7 us; splitting
+    c1's K = 256 projections too, whose residual sites then run their
+    LayerNorm in the reduce kernel, takes c1 from 0.070 to 0.067 ms)."""
     tiles = -(-m // 128) * -(-n // 64)
-    return 0 if k >= 512 and tiles * 4 < sms else None
+    return 0 if k >= 256 and tiles * 4 < sms else None
 
 
 # FFN row chunking (torch_transformer_benchmark.py:3841-3938): when the
