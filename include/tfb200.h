@@ -184,16 +184,6 @@ int tf_gemm_residual_splitk(const void* A, int64_t lda, const void* W, int64_t l
                             int64_t M, int64_t N, int64_t K, int splits, void* workspace, int64_t workspace_bytes,
                             void* stream);
 
-/* The GEMM of tf_gemm_splitk without its reduce: the result is the fp32
- * partial sums themselves, workspace = [splits][M][N] (no bias), for a
- * consumer that sums them in split order as part of its own work
- * (tf_short_attention). epilogue: 0 or TF_EPI_BF16 (the operand type only).
- * *splits_used receives the number of partial planes written. Same
- * projection as tf_gemm_splitk (torch_transformer_benchmark.py:4138-4143). */
-int tf_gemm_splitk_partials(const void* A, int64_t lda, const void* W, int64_t ldw, int64_t M, int64_t N, int64_t K,
-                            int epilogue, int splits, void* workspace, int64_t workspace_bytes, int* splits_used,
-                            void* stream);
-
 /* tf_gemm_residual_splitk whose reduce kernel also runs the LayerNorm of the
  * result (one warp per row):
  *   x_out  = as tf_gemm_residual_splitk
@@ -250,23 +240,6 @@ int tf_flash_fwd(const void* q, const void* k, const void* v, int64_t ld_q, int6
                  int64_t bs_kv, void* out, int64_t ld_o, int64_t bs_o, float* lse, const uint8_t* key_valid,
                  int64_t batch, int64_t heads, int64_t seq_q, int64_t seq_k, int64_t head_dim, float scale,
                  int64_t q_pos0, int64_t k_pos0, int flags, void* stream);
-
-/* Attention of short sequences (seq <= 128 tokens, head_dim 64, fp16
- * operands) in one CTA per (batch element, head):
- *   out[b, i, h*64:(h+1)*64] = sum_j softmax_j(scale * q_i . k_j) v_j
- * with q|k|v either packed fp16 rows qkv [batch*seq][3*heads*64] (part =
- * NULL) or the fp32 partials of tf_gemm_splitk_partials on the QKV
- * projection, part [splits][batch*seq][3*heads*64], summed in split order
- * plus bias [3*heads*64] and rounded to fp16 (qkv = NULL). key_valid: uint8
- * [batch][seq] (nonzero = key may be attended) or NULL; flags:
- * TF_ATTN_CAUSAL. out: fp16 with token pitch ld_o; a row whose keys are all
- * masked gets 0. Replaces the reference's short-sequence attention
- * (_short_attn_kernel / _triton_short_attention, torch_transformer_benchmark.py:
- * 1193-1304, 1596-1625), and, fed from the partials, the split-K reduce of the
- * QKV projection before it. */
-int tf_short_attention(const float* part, int splits, const float* bias, const void* qkv, const uint8_t* key_valid,
-                       void* out, int64_t ld_o, int64_t batch, int64_t heads, int64_t seq, int64_t head_dim,
-                       float scale, int flags, void* stream);
 
 /* Merge one partial attention result into a running one (log-sum-exp
  * combination, exact): with L = logaddexp(lse_acc, lse_part)

@@ -172,8 +172,6 @@ def _record_schedule(monkeypatch, cfg, m_rows, chunk_budget=None):
     monkeypatch.setattr(K, "linear_residual", rec("res", lambda a, w, b, x_in, x_out, *r, **kw: x_out))
     monkeypatch.setattr(K, "linear_residual_ln",
                         rec("res_ln", lambda a, w, b, x_in, x_out, *r, **kw: (x_out, torch.zeros(1))))
-    monkeypatch.setattr(K, "linear_partials", rec("partials", lambda *a, **kw: 3))
-    monkeypatch.setattr(K, "short_attention", rec("short", lambda *a, **kw: None))
     model = UserOptimizedTransformer(cfg)
     model.ffn_chunk_budget_bytes = chunk_budget
     model._forward_core(torch.zeros(1, m_rows, cfg.d_model), None, False)
@@ -181,16 +179,14 @@ def _record_schedule(monkeypatch, cfg, m_rows, chunk_budget=None):
 
 
 def test_forward_schedule_few_rows(monkeypatch):
-    """c2 (64 rows): every projection takes the split-K form, the QKV
-    projection's partials feed the short-sequence attention directly, and
-    each residual site runs the following LayerNorm in its reduce kernel (the
-    next layer's norm1, the final norm after the last layer, fp32 out)."""
+    """c2 (64 rows): every projection takes the split-K form and each
+    residual site runs the following LayerNorm in its reduce kernel (the next
+    layer's norm1, the final norm after the last layer, fp32 out)."""
     cfg = NAMED_CONFIGS["c2"]
     calls = _record_schedule(monkeypatch, cfg, 64)
     names = [c[0] for c in calls]
-    assert names == ["ln"] + ["partials", "short", "res_ln", "linear", "res_ln"] * cfg.num_layers
+    assert names == ["ln"] + ["linear", "flash", "res_ln", "linear", "res_ln"] * cfg.num_layers
     assert all(kw.get("splits") == 0 for n, kw in calls if n in ("linear", "res_ln"))
-    assert all(kw.get("splits") == 3 and kw.get("bias") is not None for n, kw in calls if n == "short")
     assert calls[-1][1]["out_dtype"] == torch.float32 and calls[-1][1]["mask_out"] is False
 
 

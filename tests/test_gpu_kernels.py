@@ -454,73 +454,3 @@ def test_attn_merge(K):
     assert torch.allclose(oag.cpu(), ref, atol=1e-5, rtol=1e-5)
     assert torch.allclose(lag.cpu(), L, atol=1e-5)
     assert torch.allclose(o16.float().cpu(), ref, atol=2e-3, rtol=1e-3)
-
-
-@pytest.mark.parametrize("b,s,h,causal,masked,mode", [
-    (2, 128, 4, False, False, "partials"),
-    (1, 64, 8, True, False, "partials"),
-    (3, 77, 2, False, True, "partials"),
-    (2, 100, 4, True, True, "qkv"),
-    (1, 1, 2, False, False, "qkv"),
-    (4, 128, 2, True, False, "qkv"),
-])
-def test_short_attention(K, b, s, h, causal, masked, mode):
-    """tf_short_attention (S <= 128, head_dim 64) against the oracle's fp32
-    attention on the same fp16 q/k/v. With `partials` the q|k|v are three
-    fp32 split-K planes summed in split order plus the bias and rounded to
-    fp16 (what the split-K reduce would store). Same tolerance as the flash
-    kernel: P is rounded to fp16 for the PV product."""
-    g = torch.Generator().manual_seed(b * 131 + s * 7 + h)
-    d = h * 64
-    dv = _dev()
-    kv = None
-    if masked:
-        kv = torch.rand(b, s, generator=g) > 0.3
-        kv[:, 0] = True
-    if mode == "partials":
-        parts = torch.randn(3, b * s, 3 * d, generator=g) * 0.6
-        bias = torch.randn(3 * d, generator=g) * 0.1
-        qkv = ((parts[0] + parts[1] + parts[2]) + bias).half().view(b, s, 3 * d)
-    else:
-        qkv = torch.randn(b, s, 3 * d, generator=g).half()
-    q, k, v = qkv[..., :d], qkv[..., d:2 * d], qkv[..., 2 * d:]
-
-    def heads(t):
-        return t.reshape(b, s, h, 64).transpose(1, 2)
-
-    ref, _ = om.attention_fp16(heads(q), heads(k), heads(v), 0.125, causal, kv)
-    ref = ref.transpose(1, 2).reshape(b, s, d)
-    out = torch.full((b, s, d), float("nan"), dtype=torch.float16, device=dv)
-    if mode == "partials":
-        K.short_attention(h, 0.125, out, partials=parts.to(dv), splits=3, bias=bias.to(dv), causal=causal,
-                          key_valid=None if kv is None else kv.to(dv))
-    else:
-        K.short_attention(h, 0.125, out, qkv=qkv.to(dv), causal=causal, key_valid=None if kv is None else kv.to(dv))
-    torch.cuda.synchronize()
-    o = out.float().cpu()
-    assert torch.isfinite(o).all()
-    bound = 1e-2 * ref.abs() + 3e-3
-    bad = ((o - ref).abs() > bound).sum().item()
-    assert bad == 0, f"{bad} elements beyond bound, max diff {(o - ref).abs().max().item():.3g}"
-
-
-def test_linear_partials_sum_to_the_projection(K):
-    """tf_gemm_splitk_partials: the fp32 partial planes of a few-row
-    projection sum (in split order, plus the bias) to the split-K GEMM's own
-    reduce, bit for bit."""
-    g = torch.Generator().manual_seed(9)
-    dv = _dev()
-    a = (torch.randn(64, 512, generator=g)).half().to(dv)
-    w = (torch.randn(1536, 512, generator=g) / 22).half().to(dv)
-    bias = torch.randn(1536, generator=g).to(dv)
-    ws = torch.empty(K.splitk_workspace_bytes(64, 1536, 512), dtype=torch.uint8, device=dv)
-    n = K.linear_partials(a, w, ws)
-    assert n >= 2
-    parts = ws.view(torch.float32)[:n * 64 * 1536].view(n, 64, 1536).clone()
-    acc = parts[0]
-    for i in range(1, n):
-        acc = acc + parts[i]
-    mine = (acc + bias).half()
-    ref = K.linear(a, w, bias, splits=0)
-    torch.cuda.synchronize()
-    assert torch.equal(mine, ref)

@@ -56,26 +56,6 @@ def test_small_configs(name):
     _check(ref, out)
 
 
-@pytest.mark.parametrize("name,masked", [("c1", False), ("c1_causal", True), ("c2", True), ("c2_causal", False)])
-def test_short_attention_path(name, masked):
-    """Sequences of at most 128 tokens: the QKV projection's split-K partials
-    feed tf_short_attention directly. The output passes the gate against the
-    oracle and stays within 2e-3 of the QKV reduce + flash kernel path."""
-    cfg = SMALL[name]
-    p, x, model = _build(cfg, seed=5)
-    mask = None
-    if masked:
-        mask = om.padded_mask(cfg, 0.4, 99)
-        x = x.masked_fill(~mask[..., None], 0)
-    xg, mg = x.cuda(), (mask.cuda() if masked else None)
-    with torch.inference_mode():
-        short = model(xg, mg)
-        model.short_attention = False
-        flash = model(xg, mg)
-    _check(om.forward(p, cfg, x, mask), short)
-    assert float((short - flash).abs().max()) < 2e-3
-
-
 @pytest.mark.parametrize("causal", [False, True])
 def test_partial_mask(causal):
     cfg = TransformerConfig(3, 200, 256, 4, 1024, 2, causal)

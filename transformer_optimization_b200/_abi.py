@@ -73,8 +73,6 @@ SIGNATURES = {
     "tf_gemm_residual_splitk": ([_P, _I64, _P, _I64, _P, _P, _P, _I64, _P, _I, _I64, _I64, _I64, _I, _P, _I64, _P],
                                 _I),
     "tf_gemm_splitk_static": ([_P, _I64, _P, _I64, _P, _P, _I64, _I64, _I64, _I64, _I, _I, _P], _I),
-    "tf_gemm_splitk_partials": ([_P, _I64, _P, _I64, _I64, _I64, _I64, _I, _I, _P, _I64, ctypes.POINTER(_I), _P], _I),
-    "tf_short_attention": ([_P, _I, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _F, _I, _P], _I),
     "tf_gemm_residual_ln_splitk": ([_P, _I64, _P, _I64, _P, _P, _P, _I64, _P, _I, _I64, _I64, _I64, _I, _P, _I64,
                                     _P, _P, _F, _P, _I, _P], _I),
 }

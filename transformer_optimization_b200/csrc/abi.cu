@@ -338,50 +338,6 @@ int tf_gemm_splitk(const void* A, int64_t lda, const void* W, int64_t ldw, const
   return tfb::gemm_splitk_f16(g, splits, static_cast<float*>(workspace), workspace_bytes, as_stream(stream));
 }
 
-int tf_gemm_splitk_partials(const void* A, int64_t lda, const void* W, int64_t ldw, int64_t M, int64_t N, int64_t K,
-                            int epilogue, int splits, void* workspace, int64_t workspace_bytes, int* splits_used,
-                            void* stream) {
-  int rc = begin_call();
-  if (rc) return rc;
-  if (splits_used == nullptr) return set_error(TF_ERR_SHAPE, "tf_gemm_splitk_partials: splits_used is NULL");
-  if (epilogue & ~TF_EPI_BF16) return set_error(TF_ERR_SHAPE, "tf_gemm_splitk_partials: epilogue=%d", epilogue);
-  tfb::GemmCall g = {};
-  g.A = A;
-  g.lda = lda;
-  g.W = W;
-  g.ldw = ldw;
-  g.M = M;
-  g.N = N;
-  g.K = K;
-  g.epilogue = 0;
-  g.dtype = (epilogue & TF_EPI_BF16) ? tfb::kDtBF16 : tfb::kDtF16;
-  g.a_repeat = 1;
-  return tfb::gemm_splitk_f16(g, splits, static_cast<float*>(workspace), workspace_bytes, as_stream(stream), nullptr,
-                              splits_used);
-}
-
-int tf_short_attention(const float* part, int splits, const float* bias, const void* qkv, const uint8_t* key_valid,
-                       void* out, int64_t ld_o, int64_t batch, int64_t heads, int64_t seq, int64_t head_dim,
-                       float scale, int flags, void* stream) {
-  int rc = begin_call();
-  if (rc) return rc;
-  tfb::ShortAttnArgs a;
-  a.part = part;
-  a.splits = splits;
-  a.bias = bias;
-  a.qkv = qkv;
-  a.key_valid = key_valid;
-  a.out = out;
-  a.ld_o = ld_o;
-  a.batch = batch;
-  a.heads = heads;
-  a.seq = seq;
-  a.head_dim = head_dim;
-  a.scale = scale;
-  a.flags = flags;
-  return tfb::short_attention(a, as_stream(stream));
-}
-
 int tf_gemm_splitk_static(const void* A, int64_t lda, const void* W, int64_t ldw, const float* bias, void* C,
                           int64_t ldc, int64_t M, int64_t N, int64_t K, int epilogue, int splits, void* stream) {
   int rc = begin_call();

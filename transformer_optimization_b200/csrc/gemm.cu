@@ -973,7 +973,7 @@ long long gemm_splitk_workspace_bytes(long long M, long long N, long long K, int
 }
 
 int gemm_splitk_f16(const GemmCall& g, int splits_req, float* ws, long long ws_bytes, cudaStream_t stream,
-                    const LnFuse* ln, int* splits_out) {
+                    const LnFuse* ln) {
   const long long M = g.M, N = g.N, K = g.K;
   if (M <= 0 || N <= 0 || K <= 0) return set_error(TF_ERR_SHAPE, "gemm_splitk: empty shape M=%lld N=%lld K=%lld", M, N, K);
   if (M > (1ll << 31) - 1 || N > 65535ll * 64 || K > (1 << 24)) return set_error(TF_ERR_SHAPE, "gemm_splitk: shape out of range");
@@ -985,8 +985,8 @@ int gemm_splitk_f16(const GemmCall& g, int splits_req, float* ws, long long ws_b
   if (K % 8 != 0 || g.lda % 8 != 0 || g.ldw % 8 != 0)
     return set_error(TF_ERR_ALIGN, "gemm_splitk: K and leading dimensions must be multiples of 8 elements");
   if (g.lda < K || g.ldw < K) return set_error(TF_ERR_SHAPE, "gemm_splitk: leading dimension smaller than row");
-  if (!aligned16(g.A) || !aligned16(g.W) || g.A == nullptr || g.W == nullptr ||
-      (splits_out == nullptr && (g.bias == nullptr || !aligned16(g.bias))))
+  if (!aligned16(g.A) || !aligned16(g.W) || !aligned16(g.bias) || g.A == nullptr || g.W == nullptr ||
+      g.bias == nullptr)
     return set_error(TF_ERR_ALIGN, "gemm_splitk: A, W and bias must be non-null and 16-byte aligned");
   if (g.epilogue == 2 || g.epilogue == 4) {
     const int mult = g.epilogue == 2 ? 4 : 8;
@@ -996,7 +996,7 @@ int gemm_splitk_f16(const GemmCall& g, int splits_req, float* ws, long long ws_b
                        "gemm_splitk: x_in/x_out must be 16-byte aligned with a pitch >= N, multiple of %d", mult);
     if (g.mask_mode < 0 || g.mask_mode > 2) return set_error(TF_ERR_SHAPE, "gemm_splitk: mask mode %d", g.mask_mode);
     if (g.mask_mode != 0 && g.valid == nullptr) return set_error(TF_ERR_SHAPE, "gemm_splitk: mask without valid rows");
-  } else if (splits_out == nullptr && (g.C == nullptr || !aligned16(g.C) || g.ldc % 8 != 0 || g.ldc < N)) {
+  } else if (g.C == nullptr || !aligned16(g.C) || g.ldc % 8 != 0 || g.ldc < N) {
     return set_error(TF_ERR_ALIGN, "gemm_splitk: C must be 16-byte aligned with a pitch >= N, multiple of 8");
   }
   if (ln != nullptr) {
@@ -1039,10 +1039,6 @@ int gemm_splitk_f16(const GemmCall& g, int splits_req, float* ws, long long ws_b
   rc = g.dtype == kDtBF16 ? launch_gemm_cfg<64, 8, 3, kDtBF16>(ta, tb, args, grid, stream)
                           : launch_gemm_cfg<64, 8, 3, kDtF16>(ta, tb, args, grid, stream);
   if (rc) return rc;
-  if (splits_out != nullptr) {  // the partials are the result: their consumer sums them
-    *splits_out = splits;
-    return TF_OK;
-  }
 
   if (ln != nullptr) {
     // one block per row

@@ -102,10 +102,8 @@ struct LnFuse {
 int gemm_f16(const GemmCall& g, cudaStream_t stream);
 // split-K GEMM (epilogues 0, 1, 2, 4, 5) with an fp32 partial-sum workspace;
 // with `ln` (residual epilogues) the reduce kernel also runs that LayerNorm
-// with splits_out the reduce is not launched: the fp32 partials [splits][M][N]
-// (no bias) are the result and *splits_out their count
 int gemm_splitk_f16(const GemmCall& g, int splits, float* ws, long long ws_bytes, cudaStream_t stream,
-                    const LnFuse* ln = nullptr, int* splits_out = nullptr);
+                    const LnFuse* ln = nullptr);
 long long gemm_splitk_workspace_bytes(long long M, long long N, long long K, int splits);
 // the same with the library's fixed 4 MiB device scratch (no allocation)
 int gemm_splitk_static_f16(const GemmCall& g, int splits, cudaStream_t stream);
@@ -143,23 +141,6 @@ struct MergeArgs {
 };
 
 int attn_merge(const MergeArgs& a, cudaStream_t stream);
-
-// attention of short sequences (S <= 128, head_dim 64) in one CTA per
-// (batch, head), from split-K partials of the QKV projection or packed fp16
-// q|k|v (short_attn.cu)
-struct ShortAttnArgs {
-  const float* part;  // [splits][batch*seq][3*heads*64] fp32 partial sums, or nullptr
-  int splits;
-  const float* bias;  // [3*heads*64] fp32 (with part)
-  const void* qkv;    // [batch*seq][3*heads*64] fp16 (without part)
-  const uint8_t* key_valid;  // [batch][seq] or nullptr
-  void* out;          // fp16, token pitch ld_o
-  long long ld_o;
-  long long batch, heads, seq, head_dim;
-  float scale;
-  int flags;  // TF_ATTN_CAUSAL
-};
-int short_attention(const ShortAttnArgs& a, cudaStream_t stream);
 
 // test probe of the bounded waits (probe.cu)
 int wait_timeout_probe(const void* src, long long limit_ns, int* out, cudaStream_t stream);

@@ -10,8 +10,6 @@ from __future__ import annotations
 
 from typing import Optional, Tuple
 
-import ctypes
-
 import torch
 
 from . import _abi
@@ -352,56 +350,4 @@ def wait_timeout_probe(src: torch.Tensor, limit_ns: int) -> torch.Tensor:
         raise ValueError("wait_timeout_probe: src must be contiguous with at least 4096 bytes")
     out = torch.full((3,), -7, dtype=torch.int32, device=src.device)
     _abi.call("tf_test_wait_timeout", _ptr(src), int(limit_ns), _ptr(out), _stream())
-    return out
-
-
-def linear_partials(a: torch.Tensor, w: torch.Tensor, workspace: torch.Tensor, splits: int = 0) -> int:
-    """The split-K GEMM of `linear` without its reduce
-    (tf_gemm_splitk_partials): workspace receives the fp32 partial sums
-    [splits][rows][N] of a @ w.T (no bias). Returns the number of splits."""
-    _need_cuda("linear_partials", a, w, workspace)
-    if a.dtype not in HALF_TYPES or w.dtype != a.dtype:
-        raise ValueError("linear_partials: a and w must both be fp16 or both bf16")
-    k = a.shape[-1]
-    a2 = a.reshape(-1, k)
-    if a2.stride(-1) != 1 or w.stride(-1) != 1 or w.shape[1] != k:
-        raise ValueError("linear_partials: operands [rows, K] and [N, K] with unit inner stride")
-    used = ctypes.c_int(0)
-    epi = _abi.TF_EPI_BF16 if a.dtype == torch.bfloat16 else 0
-    _abi.call("tf_gemm_splitk_partials", _ptr(a2), a2.stride(0), _ptr(w), w.stride(0), a2.shape[0], w.shape[0], k,
-              epi, int(splits), _ptr(workspace), workspace.numel() * workspace.element_size(), ctypes.byref(used),
-              _stream())
-    return used.value
-
-
-def short_attention(heads: int, scale: float, out: torch.Tensor, *, qkv: Optional[torch.Tensor] = None,
-                    partials: Optional[torch.Tensor] = None, splits: int = 0, bias: Optional[torch.Tensor] = None,
-                    causal: bool = False, key_valid: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """Attention of sequences of at most 128 tokens, head_dim 64, one CTA
-    per (batch element, head) (tf_short_attention). out: fp16 [B, S, H*64]
-    with unit inner stride. q|k|v from `qkv` (fp16 [B, S, 3*H*64],
-    contiguous) or from the fp32 split-K `partials` of the QKV projection
-    (linear_partials' workspace, `splits` planes) plus `bias` (fp32)."""
-    _need_cuda("short_attention", out, qkv, partials, bias, key_valid)
-    if out.dtype != torch.float16 or out.dim() != 3 or out.stride(-1) != 1:
-        raise ValueError("short_attention: out must be fp16 [B, S, H*64] with unit inner stride")
-    bsz, seq, d = out.shape
-    if d != heads * 64:
-        raise ValueError("short_attention: head_dim 64 only")
-    if (qkv is None) == (partials is None):
-        raise ValueError("short_attention: give either qkv or partials")
-    if qkv is not None and (qkv.dtype != torch.float16 or not qkv.is_contiguous() or qkv.shape != (bsz, seq, 3 * d)):
-        raise ValueError("short_attention: qkv must be contiguous fp16 [B, S, 3*H*64]")
-    if partials is not None:
-        if bias is None or bias.dtype != torch.float32 or bias.numel() != 3 * d or splits < 1:
-            raise ValueError("short_attention: partials need the fp32 bias [3*H*64] and their split count")
-        if partials.numel() * partials.element_size() < splits * bsz * seq * 3 * d * 4:
-            raise ValueError("short_attention: partials smaller than splits x rows x 3*H*64 fp32")
-    if key_valid is not None:
-        if key_valid.shape != (bsz, seq) or key_valid.dtype not in (torch.bool, torch.uint8):
-            raise ValueError("short_attention: key_valid must be bool [B, S]")
-        key_valid = key_valid.contiguous()
-    flags = _abi.TF_ATTN_CAUSAL if causal else 0
-    _abi.call("tf_short_attention", _ptr(partials), int(splits), _ptr(bias), _ptr(qkv), _ptr(key_valid), _ptr(out),
-              out.stride(1), bsz, heads, seq, 64, float(scale), flags, _stream())
     return out

@@ -228,11 +228,6 @@ class UserOptimizedTransformer(BaselineTransformer):
         # 173); False keeps fp32 scores (closer to the fp32 model, further
         # from eager T)
         self.round_half_scores = True
-        # few-row fp32 forwards with sequences of at most 128 tokens (head_dim
-        # 64): the QKV projection leaves its split-K partials and one short-
-        # attention kernel per (batch, head) sums them and attends
-        # (tf_short_attention), one launch instead of reduce + flash
-        self.short_attention = True
 
     def _model_dtype(self) -> torch.dtype:
         return self.final_norm.weight.dtype
@@ -328,7 +323,6 @@ class UserOptimizedTransformer(BaselineTransformer):
                 ws = self._splitk_ws = torch.empty(need, dtype=torch.uint8, device=dev)
         self._last_ws_used = ws is not None
 
-        short = (self.short_attention and not half and sk_qkv is not None and s <= 128 and d == 64 * h)
         # With split-K residual projections (few rows), their reduce kernel also
         # runs the LayerNorm that follows (the next layer's norm1, or the final
         # norm after the last layer): one launch fewer per residual site.
@@ -340,15 +334,10 @@ class UserOptimizedTransformer(BaselineTransformer):
             w = wts[li]
             if not normed_ready:
                 kernels.ln_residual(cur, None, w.n1w, w.n1b, blk.norm1.eps, normed=normed)
-            if short:
-                nsp = kernels.linear_partials(normed, w.wqkv, ws)
-                kernels.short_attention(h, scale, ctx, partials=ws, splits=nsp, bias=w.bqkv, causal=cfg.causal,
-                                        key_valid=kvalid)
-            else:
-                kernels.linear(normed, w.wqkv, w.bqkv, out=qkv, splits=sk_qkv, workspace=ws)
-                kernels.flash_attention(qkv[..., :d], qkv[..., d:2 * d], qkv[..., 2 * d:], h, scale,
-                                        causal=cfg.causal, key_valid=kvalid, out=ctx,
-                                        round_scores=half and self.round_half_scores)
+            kernels.linear(normed, w.wqkv, w.bqkv, out=qkv, splits=sk_qkv, workspace=ws)
+            kernels.flash_attention(qkv[..., :d], qkv[..., d:2 * d], qkv[..., 2 * d:], h, scale,
+                                    causal=cfg.causal, key_valid=kvalid, out=ctx,
+                                    round_scores=half and self.round_half_scores)
             if sk_o is not None:
                 cur, _ = kernels.linear_residual_ln(ctx, w.wo, w.bo, cur, x_res, vflat, w.n2w, w.n2b,
                                                     blk.norm2.eps, mask_delta=mask_active, normed=normed,
@@ -446,7 +435,7 @@ class UserOptimizedTransformer(BaselineTransformer):
         if not self.use_cuda_graphs or not self._graph_memory_safe(x):
             return self._forward_core(x, valid_token_mask, mask_active)
         key = (tuple(x.shape), x.dtype, x.device, cfg.causal, mask_kind, self._split_ffn_out(),
-               self.ffn_chunk_budget_bytes, self.round_half_scores, self.short_attention)
+               self.ffn_chunk_budget_bytes, self.round_half_scores)
         if key in self._graph_unsupported:
             return self._forward_core(x, valid_token_mask, mask_active)
         self._layer_weights()  # may invalidate cached graphs
