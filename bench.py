@@ -729,8 +729,11 @@ def main():
     if world > 1:
         import torch.distributed as dist
         torch.cuda.set_device(local_rank)
+        # high-priority NCCL streams: the ring's send/recv kernels then take
+        # the next free SMs ahead of the flash kernel's waiting CTAs
+        opts = dist.ProcessGroupNCCL.Options(is_high_priority_stream=True)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", local_rank))
+                                device_id=torch.device("cuda", local_rank), pg_options=opts)
     try:
         if world > 1 and cfg.batch_size < world:
             if args.model_dtype != "float32":

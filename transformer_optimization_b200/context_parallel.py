@@ -33,6 +33,12 @@ forward's ring (CPU tensors: every exchange; CUDA tensors: the end of the
 forward, by polling an event) and then aborts the group's communicators and
 raises RingTimeout. Without it the process group's own timeout applies.
 
+NCCL's send/recv kernels need SMs of their own; while a flash kernel keeps
+every SM busy they only get one when a flash CTA exits, and at 8 ranks a
+51 MB K|V step then took longer than the flash work it should hide behind.
+Give the group high-priority NCCL streams (high_priority_nccl_options(); the
+block scheduler then runs NCCL's CTAs first when an SM frees up).
+
 The attention arithmetic is behind a small backend interface: the product
 uses `CudaAttentionBackend` (the sm_100a flash and merge kernels); the CPU
 tests drive the same ring over gloo with a host backend.
@@ -55,6 +61,12 @@ Segment = Tuple[int, int]
 class RingTimeout(RuntimeError):
     """A ring exchange did not complete within the host deadline; the
     group's communicators have been aborted."""
+
+
+def high_priority_nccl_options():
+    """Process-group options for the ring: NCCL on high-priority streams
+    (pass as pg_options to init_process_group or new_group)."""
+    return dist.ProcessGroupNCCL.Options(is_high_priority_stream=True)
 
 
 def shard_bounds(seq_len: int, world: int) -> List[Segment]:
