@@ -306,10 +306,12 @@ def e2e_pipelined(model, x_host, y_host, steps, device):
 
 def kernel_profile(model, x):
     """One instrumented eager forward: CUDA events around every launch of the
-    GEMM, attention and LayerNorm kernels (on the launching stream).
+    GEMM, attention and LayerNorm kernels (on the launching stream). The
+    events serialise the launches, so a LayerNorm that overlaps its residual
+    GEMM's tail in the graph (ln_ready) is timed here on its own.
     Returns {kernel: (launches, total_ms, algorithmic units)}."""
     rec = {"gemm": [], "flash": [], "ln": []}
-    orig = (K.linear, K.flash_attention, K.ln_residual, K.linear_residual, K.linear_residual_ln)
+    orig = (K.linear, K.flash_attention, K.ln_residual, K.linear_residual, K.linear_residual_ln, K.ln_ready)
 
     def wrap(name, f, units):
         def g(*a, **kw):
@@ -339,11 +341,16 @@ def kernel_profile(model, x):
         by += n * (4 if kw.get("out_dtype") == torch.float32 else 2)
         return float(by)
 
+    def ln_ready_bytes(x, w, b, eps, ready, valid=None, **kw):
+        n = x.numel()
+        return float(n * x.element_size() + n * (4 if kw.get("out_dtype") == torch.float32 else 2))
+
     K.linear = wrap("gemm", orig[0], gemm_flops)
     K.flash_attention = wrap("flash", orig[1], flash_flops)
     K.ln_residual = wrap("ln", orig[2], ln_bytes)
     K.linear_residual = wrap("gemm", orig[3], gemm_flops)
     K.linear_residual_ln = wrap("gemm", orig[4], gemm_flops)
+    K.ln_ready = wrap("ln", orig[5], ln_ready_bytes)
     try:
         model.use_cuda_graphs = False
         with torch.inference_mode():
@@ -360,7 +367,7 @@ def kernel_profile(model, x):
             model(x)
         torch.cuda.synchronize()
     finally:
-        K.linear, K.flash_attention, K.ln_residual, K.linear_residual, K.linear_residual_ln = orig
+        K.linear, K.flash_attention, K.ln_residual, K.linear_residual, K.linear_residual_ln, K.ln_ready = orig
         model.use_cuda_graphs = True
     out = {}
     for name, lst in rec.items():

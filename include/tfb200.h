@@ -164,6 +164,30 @@ int tf_gemm_residual(const void* A, int64_t lda, const void* W, int64_t ldw, con
                      const void* x_in, void* x_out, int64_t ldx, const uint8_t* valid, int mask_mode,
                      int64_t M, int64_t N, int64_t K, int w_split, int tile_n, int pair, void* stream);
 
+/* A residual GEMM and the LayerNorm of its output running at the same time.
+ * tf_gemm_residual_ready is tf_gemm_residual (automatic tiling, x_out
+ * contiguous: ldx == N) whose epilogue also adds, for every group of 8 rows,
+ * the number of x_out columns it has stored to ready[group]; a group is
+ * complete when its count reaches N. ready: int32[ceil(M / 8)] device array,
+ * all zero before the call.
+ * tf_ln_ready is tf_ln_residual without delta (normed = mask_out(LayerNorm(x)
+ * * w + b); flags TF_LN_MASK_OUT, TF_LN_OUT_F32, TF_LN_X_F16, TF_LN_X_BF16;
+ * D <= 2048) for x being written by a tf_gemm_residual_ready launched just
+ * before it on the same stream with the same ready array and N == D: it waits
+ * per row group for the count D instead of for the GEMM to finish, so its
+ * CTAs run on the SMs the GEMM's last, partial wave leaves idle; each count
+ * it consumes is set back to 0, so the array is ready for the next pair.
+ * After a failed call (or a device timeout) zero the array again. A count
+ * that never completes ends in device code 107 after the 2 s wait bound.
+ * Replaces out_proj / ffn_out with the residual add and the LayerNorm of the
+ * following _ln_site (torch_transformer_benchmark.py:4163-4169, 4194,
+ * 3940-4001) or the final LayerNorm (4316-4325). */
+int tf_gemm_residual_ready(const void* A, int64_t lda, const void* W, int64_t ldw, const float* bias,
+                           const void* x_in, void* x_out, int64_t ldx, const uint8_t* valid, int mask_mode,
+                           int64_t M, int64_t N, int64_t K, int w_split, int* ready, void* stream);
+int tf_ln_ready(const void* x, const float* w, const float* b, float eps, const uint8_t* valid, int64_t M,
+                int64_t D, int flags, void* normed, int* ready, void* stream);
+
 /* Split-K forms of tf_gemm / tf_gemm_residual for few-row inputs (small
  * batch x sequence), where 128-row tiles leave most SMs idle: each tile's
  * K range is cut into `splits` parts (splits <= 0: automatic, about one work

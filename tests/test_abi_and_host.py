@@ -57,7 +57,7 @@ def test_header_symbols_exported(lib):
 
 
 def test_abi_version_and_error_string(lib):
-    assert lib.tf_abi_version() == 10
+    assert lib.tf_abi_version() == 11
     assert isinstance(lib.tf_last_error(), bytes)
 
 
@@ -149,7 +149,7 @@ def test_bench_algorithmic_bytes():
     assert 140e6 < bench.C3_GEMM_DRAM_BYTES_PER_LAUNCH < expect  # measured DRAM bytes below algorithmic
 
 
-def _record_schedule(monkeypatch, cfg, m_rows, chunk_budget=None):
+def _record_schedule(monkeypatch, cfg, m_rows, chunk_budget=None, overlap_ln=True):
     """Run the model's per-layer schedule with the kernel wrappers replaced
     by recorders (no GPU): returns [(wrapper, kwargs)] in call order."""
     import types
@@ -172,8 +172,11 @@ def _record_schedule(monkeypatch, cfg, m_rows, chunk_budget=None):
     monkeypatch.setattr(K, "linear_residual", rec("res", lambda a, w, b, x_in, x_out, *r, **kw: x_out))
     monkeypatch.setattr(K, "linear_residual_ln",
                         rec("res_ln", lambda a, w, b, x_in, x_out, *r, **kw: (x_out, torch.zeros(1))))
+    monkeypatch.setattr(K, "ln_ready", rec("ln_ready", lambda x, *a, **kw: torch.zeros(1)))
+    monkeypatch.setattr(K, "ready_counters", lambda rows, dev: torch.zeros((rows + 7) // 8, dtype=torch.int32))
     model = UserOptimizedTransformer(cfg)
     model.ffn_chunk_budget_bytes = chunk_budget
+    model.overlap_ln = overlap_ln
     model._forward_core(torch.zeros(1, m_rows, cfg.d_model), None, False)
     return calls
 
@@ -191,13 +194,26 @@ def test_forward_schedule_few_rows(monkeypatch):
 
 
 def test_forward_schedule_many_rows(monkeypatch):
-    """c3-sized rows: no split-K; residual sites in the GEMM epilogue, then a
-    LayerNorm kernel each, and the final LayerNorm."""
+    """c3-sized rows: no split-K; residual sites in the GEMM epilogue, each
+    followed by a LayerNorm that overlaps the GEMM's tail through the same
+    ready counters (norm2, the next layer's norm1, the final norm in fp32)."""
     cfg = TransformerConfig(8, 2048, 1024, 16, 4096, 2, False)
     calls = _record_schedule(monkeypatch, cfg, 8 * 2048)  # the 16 384 rows as one sequence
     names = [c[0] for c in calls]
-    assert names == ["ln", "linear", "flash", "res", "ln", "linear", "res"] * cfg.num_layers + ["ln"]
+    assert names == ["ln"] + ["linear", "flash", "res", "ln_ready", "linear", "res", "ln_ready"] * cfg.num_layers
     assert all(kw.get("splits") is None for n, kw in calls if n == "linear")
+    readies = [kw["ready"] for n, kw in calls if n == "res"]
+    assert all(r is readies[0] and r.numel() == 8 * 2048 // 8 for r in readies)
+    assert calls[-1][1]["out_dtype"] == torch.float32 and calls[-1][1]["mask_out"] is False
+
+
+def test_forward_schedule_many_rows_no_overlap(monkeypatch):
+    """overlap_ln = False: each LayerNorm runs after its GEMM has finished."""
+    cfg = TransformerConfig(8, 2048, 1024, 16, 4096, 2, False)
+    calls = _record_schedule(monkeypatch, cfg, 8 * 2048, overlap_ln=False)
+    names = [c[0] for c in calls]
+    assert names == ["ln", "linear", "flash", "res", "ln", "linear", "res"] * cfg.num_layers + ["ln"]
+    assert all(kw.get("ready") is None for n, kw in calls if n == "res")
 
 
 def test_ffn_chunk_decision():

@@ -147,6 +147,29 @@ def test_chunked_ffn_is_bit_identical(masked):
     _check(om.forward(p, cfg, x, mask), chunked)
 
 
+@pytest.mark.parametrize("masked", [False, True])
+def test_overlapped_layernorm_is_bit_identical(masked):
+    """The LayerNorm sites that start under their residual GEMM's tail (ready
+    counters) give the same bits as the ones run after the GEMM, in a graph
+    and eagerly, and the forward passes the gate."""
+    cfg = TransformerConfig(4, 1024, 1024, 16, 4096, 2, True)
+    p, x, model = _build(cfg, seed=9)
+    mask = om.padded_mask(cfg, 0.3, 5) if masked else None
+    if masked:
+        x = x.masked_fill(~mask[..., None], 0)
+    xg, mg = x.cuda(), (mask.cuda() if masked else None)
+    with torch.inference_mode():
+        a = model(xg, mg)
+        model.overlap_ln = False
+        b = model(xg, mg)
+        model.use_cuda_graphs = False
+        model.overlap_ln = True
+        c = model(xg, mg)
+        d = model(xg, mg)
+    assert torch.equal(a, b) and torch.equal(a, c) and torch.equal(a, d)
+    _check(om.forward(p, cfg, x, mask), a)
+
+
 def test_weight_reload_invalidates_caches():
     cfg = NAMED_CONFIGS["c1"]
     p, x, model = _build(cfg)

@@ -65,6 +65,8 @@ SIGNATURES = {
     "tf_gemm": ([_P, _I64, _P, _I64, _P, _P, _I64, _I64, _I64, _I64, _I, _P], _I),
     "tf_gemm_tiled": ([_P, _I64, _P, _I64, _P, _P, _I64, _I64, _I64, _I64, _I, _I, _I, _P], _I),
     "tf_gemm_residual": ([_P, _I64, _P, _I64, _P, _P, _P, _I64, _P, _I, _I64, _I64, _I64, _I, _I, _I, _P], _I),
+    "tf_gemm_residual_ready": ([_P, _I64, _P, _I64, _P, _P, _P, _I64, _P, _I, _I64, _I64, _I64, _I, _P, _P], _I),
+    "tf_ln_ready": ([_P, _P, _P, _F, _P, _I64, _I64, _I, _P, _P, _P], _I),
     "tf_flash_fwd": ([_P, _P, _P, _I64, _I64, _I64, _I64, _P, _I64, _I64, _P, _P,
                       _I64, _I64, _I64, _I64, _I64, _F, _I64, _I64, _I, _P], _I),
     "tf_attn_merge": ([_P, _P, _P, _P, _I64, _I64, _P, _I64, _I64, _I64, _I64, _I64, _I64, _P], _I),

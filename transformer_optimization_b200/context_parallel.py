@@ -372,20 +372,40 @@ class ContextParallelTransformer:
         scale = (d // h) ** -0.5
         wts = m._layer_weights()
         x_res, normed, qkv, ctx, hidden = self._buffers(b, s_loc, d, cfg.ffn_dim, dev)
+        # residual GEMM -> LayerNorm pairs overlap as in the single-GPU forward
+        ready = kernels.ready_counters(b * s_loc, dev) if (m.overlap_ln and d <= 2048) else None
+        fn = m.final_norm
         cur = x_local
+        out = None
+        normed_ready = False
+        n_layers = len(m.layers)
         for li, blk in enumerate(m.layers):
             w = wts[li]
-            kernels.ln_residual(cur, None, w.n1w, w.n1b, blk.norm1.eps, normed=normed)
+            if not normed_ready:
+                kernels.ln_residual(cur, None, w.n1w, w.n1b, blk.norm1.eps, normed=normed)
             kernels.linear(normed, w.wqkv, w.bqkv, out=qkv)
             self.ring(qkv[..., :d], qkv[..., d:2 * d], qkv[..., 2 * d:], h, scale, cfg.causal, layout, ctx,
                       mask_full)
-            cur = kernels.linear_residual(ctx, w.wo, w.bo, cur, x_res, vflat, mask_delta=active)
-            kernels.ln_residual(cur, None, w.n2w, w.n2b, blk.norm2.eps, normed=normed)
+            cur = kernels.linear_residual(ctx, w.wo, w.bo, cur, x_res, vflat, mask_delta=active, ready=ready)
+            if ready is not None:
+                kernels.ln_ready(cur, w.n2w, w.n2b, blk.norm2.eps, ready, normed=normed)
+            else:
+                kernels.ln_residual(cur, None, w.n2w, w.n2b, blk.norm2.eps, normed=normed)
             kernels.linear(normed, w.w1, w.b1, gelu=True, out=hidden)
-            kernels.linear_residual(hidden, w.w2, w.b2, cur, x_res, vflat, mask_x=active, w_split=w.split_w2)
-        fn = m.final_norm
-        _, out = kernels.ln_residual(cur, None, fn.weight, fn.bias, fn.eps, vflat, mask_out=active,
-                                     out_dtype=torch.float32)
+            kernels.linear_residual(hidden, w.w2, w.b2, cur, x_res, vflat, mask_x=active, w_split=w.split_w2,
+                                    ready=ready)
+            if ready is None:
+                continue
+            if li + 1 < n_layers:
+                wn, nxt = wts[li + 1], m.layers[li + 1]
+                kernels.ln_ready(cur, wn.n1w, wn.n1b, nxt.norm1.eps, ready, normed=normed)
+                normed_ready = True
+            else:
+                out = kernels.ln_ready(cur, fn.weight, fn.bias, fn.eps, ready, vflat, mask_out=active,
+                                       out_dtype=torch.float32)
+        if out is None:
+            _, out = kernels.ln_residual(cur, None, fn.weight, fn.bias, fn.eps, vflat, mask_out=active,
+                                         out_dtype=torch.float32)
         if self.deadline_s is not None:
             self._await(dev)
         return out

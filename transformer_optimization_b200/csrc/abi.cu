@@ -166,7 +166,7 @@ static inline int begin_call() {
 
 extern "C" {
 
-int tf_abi_version(void) { return 10; }
+int tf_abi_version(void) { return 11; }
 
 const char* tf_last_error(void) { return tfb::g_msg; }
 
@@ -273,11 +273,10 @@ int tf_gemm_tiled(const void* A, int64_t lda, const void* W, int64_t ldw, const 
   return gemm_common(A, lda, W, ldw, bias, C, ldc, M, N, K, epilogue, tile_n, pair, stream);
 }
 
-int tf_gemm_residual(const void* A, int64_t lda, const void* W, int64_t ldw, const float* bias,
-                     const void* x_in, void* x_out, int64_t ldx, const uint8_t* valid, int mask_mode,
-                     int64_t M, int64_t N, int64_t K, int w_split, int tile_n, int pair, void* stream) {
-  int rc = begin_call();
-  if (rc) return rc;
+static int gemm_residual_common(const void* A, int64_t lda, const void* W, int64_t ldw, const float* bias,
+                                const void* x_in, void* x_out, int64_t ldx, const uint8_t* valid, int mask_mode,
+                                int64_t M, int64_t N, int64_t K, int w_split, int tile_n, int pair, int* ready,
+                                void* stream) {
   int epi = 0, mask = 0, dtype = 0;
   if (!residual_mode(mask_mode, epi, mask, dtype))
     return set_error(TF_ERR_SHAPE, "tf_gemm_residual: mask_mode=%d", mask_mode);
@@ -305,7 +304,37 @@ int tf_gemm_residual(const void* A, int64_t lda, const void* W, int64_t ldw, con
   g.a_repeat = w_split ? 2 : 1;
   g.tile_n = tile_n;
   g.pair = pair;
+  g.ready = ready;
   return tfb::gemm_f16(g, as_stream(stream));
+}
+
+int tf_gemm_residual(const void* A, int64_t lda, const void* W, int64_t ldw, const float* bias,
+                     const void* x_in, void* x_out, int64_t ldx, const uint8_t* valid, int mask_mode,
+                     int64_t M, int64_t N, int64_t K, int w_split, int tile_n, int pair, void* stream) {
+  int rc = begin_call();
+  if (rc) return rc;
+  return gemm_residual_common(A, lda, W, ldw, bias, x_in, x_out, ldx, valid, mask_mode, M, N, K, w_split, tile_n,
+                              pair, nullptr, stream);
+}
+
+int tf_gemm_residual_ready(const void* A, int64_t lda, const void* W, int64_t ldw, const float* bias,
+                           const void* x_in, void* x_out, int64_t ldx, const uint8_t* valid, int mask_mode,
+                           int64_t M, int64_t N, int64_t K, int w_split, int* ready, void* stream) {
+  int rc = begin_call();
+  if (rc) return rc;
+  if (ready == nullptr || reinterpret_cast<uintptr_t>(ready) % 4 != 0)
+    return set_error(TF_ERR_ALIGN, "tf_gemm_residual_ready: ready must be a non-null int32 array");
+  if (ldx != N) return set_error(TF_ERR_SHAPE, "tf_gemm_residual_ready: x_out must be contiguous (ldx == N)");
+  return gemm_residual_common(A, lda, W, ldw, bias, x_in, x_out, ldx, valid, mask_mode, M, N, K, w_split, 0, 0,
+                              ready, stream);
+}
+
+int tf_ln_ready(const void* x, const float* w, const float* b, float eps, const uint8_t* valid, int64_t M,
+                int64_t D, int flags, void* normed, int* ready, void* stream) {
+  int rc = begin_call();
+  if (rc) return rc;
+  if (D > (1 << 20)) return set_error(TF_ERR_SHAPE, "ln_ready: D too large");
+  return tfb::ln_ready(x, w, b, eps, valid, M, static_cast<int>(D), flags, normed, ready, as_stream(stream));
 }
 
 int64_t tf_gemm_splitk_workspace(int64_t M, int64_t N, int64_t K, int splits) {

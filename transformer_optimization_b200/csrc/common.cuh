@@ -32,6 +32,7 @@ enum DeviceError : int {
   kDevTimeoutSoftmax = 104,
   kDevTimeoutDrain = 105,
   kDevTimeoutProbe = 106,  // tf_test_wait_timeout: the wait made to run out
+  kDevReadyCount = 107,    // a row group's ready count never reached (or overshot) its target
 };
 
 // Wall-time bound of a single wait: far above any legitimate wait (the
@@ -121,6 +122,54 @@ __device__ __forceinline__ bool mbar_wait_ns(uint64_t* bar, uint32_t parity, int
 
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code) {
   return mbar_wait_ns(bar, parity, status, code, kWaitLimitNs);
+}
+
+// ---------------------------------------------------------------------------
+// Row-group ready counters: a kernel that stores rows (a residual GEMM's
+// epilogue) adds, per group of 8 rows, the number of columns it has stored;
+// a kernel running at the same time (the LayerNorm that reads those rows)
+// waits until a group's count equals the row width before reading it.
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void red_release_gpu_add(int* p, int v) {
+  asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Orders this thread's earlier generic-proxy accesses (the acquire above)
+// before its later async-proxy ones (bulk copies reading global memory).
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// Wait until *count == target (acquire). Bounded by kWaitLimitNs like every
+// other wait; a count above the target (counters not zeroed before the
+// producing kernel) is reported at once instead of read past.
+__device__ __forceinline__ bool wait_ready(const int* count, int target, int* status) {
+  int v = ld_acquire_gpu(count);
+  if (v == target) return true;
+  const uint64_t t0 = globaltimer_ns();
+  unsigned sleep_ns = 32;
+  while (true) {
+    if (v > target) {
+      record_error(status, kDevReadyCount);
+      return false;
+    }
+    __nanosleep(sleep_ns);
+    if (sleep_ns < 256) sleep_ns <<= 1;
+    v = ld_acquire_gpu(count);
+    if (v == target) return true;
+    if (error_raised(status)) return false;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      record_error(status, kDevReadyCount);
+      return false;
+    }
+  }
 }
 
 // ---------------------------------------------------------------------------

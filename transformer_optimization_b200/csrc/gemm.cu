@@ -64,6 +64,9 @@ struct GemmArgs {
   // unit goes to ws[split][M][N]. splits = 1 otherwise.
   int splits, kb_per_split;
   float* ws;
+  // EPI 2/4, optional: per 8-row group, the count of x_out columns stored so
+  // far (a group is complete at N); read by a LayerNorm that runs alongside
+  int* ready;
 };
 
 template <int BN, int STAGES>
@@ -198,6 +201,20 @@ __device__ __forceinline__ void epilogue_chunk(const GemmArgs& p, const uint32_t
 // residual epilogues (the accumulator is added to rows of x)
 template <int EPI>
 constexpr bool kResidualEpi = EPI == 2 || EPI == 4;
+
+// After a warp has stored its rows row0..row0+31 of a tile (`cols` columns of
+// x_out): add `cols` to the ready counts of the four 8-row groups. Every lane
+// fences its own stores; the counts are release adds, so a reader that
+// acquires a complete count sees every column of the group.
+__device__ __forceinline__ void signal_rows(const GemmArgs& p, int row0, int cols) {
+  __threadfence();
+  __syncwarp();
+  const int lane = threadIdx.x & 31;
+  if (lane < 4 && cols > 0) {
+    const int r = row0 + lane * 8;
+    if (r < p.M) red_release_gpu_add(p.ready + (r >> 3), cols);
+  }
+}
 
 template <int BN, int STAGES, int EPI, int DT>
 __global__ void __launch_bounds__(kGemmThreads, 1)
@@ -366,6 +383,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         const int col0 = n0 + c * 32;
         if (col0 < p.N && row0 < p.M) epilogue_chunk<EPI, DT>(p, cur, ebuf, row0, col0, xcur, sp);
+      }
+      if constexpr (kResidualEpi<EPI>) {
+        if (p.ready != nullptr && row0 < p.M) signal_rows(p, row0, p.N - n0 < BN ? p.N - n0 : BN);
       }
     }
   }
@@ -564,6 +584,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemm2Threads, 1)
         const int col0 = n0 + c * 32;
         if (col0 < p.N && row0 < p.M) epilogue_chunk<EPI, DT>(p, cur, ebuf, row0, col0, xcur);
       }
+      if constexpr (kResidualEpi<EPI>) {
+        if (p.ready != nullptr && row0 < p.M) signal_rows(p, row0, p.N - n0 < BN / 2 ? p.N - n0 : BN / 2);
+      }
     }
   }
 
@@ -649,6 +672,7 @@ static GemmArgs make_args(const GemmCall& g) {
   args.ldx = g.ldx;
   args.valid = g.valid;
   args.mask_mode = (g.epilogue == 2 || g.epilogue == 4) ? g.mask_mode : 0;
+  args.ready = (g.epilogue == 2 || g.epilogue == 4) ? g.ready : nullptr;
   args.M = static_cast<int>(g.M);
   args.N = static_cast<int>(g.N);
   args.K = static_cast<int>(g.K);

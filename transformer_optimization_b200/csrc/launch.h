@@ -87,6 +87,7 @@ struct GemmCall {
   int a_repeat;
   int tile_n;
   int pair;  // 0 automatic, 1 one-CTA tiles, 2 two-SM (CTA pair) tiles
+  int* ready;  // residual epilogues: per-8-row-group counts of stored columns, or null
 };
 
 // LayerNorm applied to the result of a residual projection (split-K form):
@@ -111,6 +112,9 @@ int gemm_splitk_static_f16(const GemmCall& g, int splits, cudaStream_t stream);
 int ln_residual(const void* x, const void* delta, const float* w, const float* b, float eps,
                 const uint8_t* valid, long long M, int D, int flags, void* x_out, void* normed,
                 cudaStream_t stream);
+// LayerNorm of rows a concurrent residual GEMM is still storing (ready mode)
+int ln_ready(const void* x, const float* w, const float* b, float eps, const uint8_t* valid, long long M, int D,
+             int flags, void* normed, int* ready, cudaStream_t stream);
 
 struct AttnArgs {
   const void* q;

@@ -24,6 +24,15 @@
 //    groups, one row per warp, and store the results straight to HBM.
 //  * ln_residual_kernel (any D up to 4096): one warp per row with the row in
 //    registers, grid-stride over rows.
+//
+// Ready mode (ln_stream_kernel, no delta): the rows come from a residual GEMM
+// that is still running (tf_gemm_residual_ready). Its epilogue counts the
+// stored columns of every 8-row group; this kernel does not wait for the GEMM
+// grid to finish (no griddepcontrol.wait) but, per group, for the group's
+// count to reach D, then copies it and zeroes the count for the next site.
+// Each CTA takes a contiguous range of groups, so the CTAs that start first
+// (on the SMs the GEMM's last, partial wave leaves idle) take the rows the
+// GEMM finished first, and the LayerNorm runs under the GEMM's tail.
 #include "common.cuh"
 #include "launch.h"
 
@@ -197,6 +206,7 @@ struct LnsParams {
   int D, flags, stages;
   float eps;
   int* status;
+  int* ready;  // ready mode: per-8-row-group stored-column counts, else null
 };
 
 // Stage ownership: group number `it` (this CTA's it-th group) goes to stage
@@ -232,8 +242,17 @@ __global__ void __launch_bounds__(lns_threads(TEAMS), 1) ln_stream_kernel(const 
     }
     fence_mbar_init();
   }
-  pdl_wait();
+  // ready mode reads only rows whose counts are complete and writes only
+  // `normed`, which no kernel still running reads
+  if (p.ready == nullptr) pdl_wait();
   pdl_trigger();
+  // this CTA's groups: strided over the grid, or (ready mode) one contiguous
+  // range, its it-th group being group_at(it)
+  const bool contiguous = p.ready != nullptr;
+  const long long g_lo = contiguous ? groups * blockIdx.x / gridDim.x : blockIdx.x;
+  const long long n_mine = contiguous ? groups * (blockIdx.x + 1) / gridDim.x - g_lo
+                                      : (groups - blockIdx.x + gridDim.x - 1) / gridDim.x;
+  auto group_at = [&](long long it) { return contiguous ? g_lo + it : g_lo + it * gridDim.x; };
   for (int i = threadIdx.x; i < (D >> 2); i += blockDim.x) {
     reinterpret_cast<float4*>(w_s)[i] = __ldg(reinterpret_cast<const float4*>(p.w) + i);
     reinterpret_cast<float4*>(b_s)[i] = __ldg(reinterpret_cast<const float4*>(p.b) + i);
@@ -243,10 +262,15 @@ __global__ void __launch_bounds__(lns_threads(TEAMS), 1) ln_stream_kernel(const 
   if (warp == kLnsRows * TEAMS) {
     // ---------------- producer ----------------
     if (lane == 0) {
-      int it = 0;
-      for (long long g = blockIdx.x; g < groups; g += gridDim.x, ++it) {
+      for (int it = 0; it < n_mine; ++it) {
+        const long long g = group_at(it);
         const int s = it % p.stages;
         if (!mbar_wait(&empty[s], ((it / p.stages) & 1) ^ 1, p.status, kDevTimeoutProducer)) break;
+        if (p.ready != nullptr) {
+          if (!wait_ready(p.ready + g, D, p.status)) break;
+          fence_proxy_async_global();
+          p.ready[g] = 0;  // consumed; the next site's GEMM starts after this grid ends
+        }
         const long long r0 = g * kLnsRows;
         const int nrows = static_cast<int>(p.M - r0 < kLnsRows ? p.M - r0 : kLnsRows);
         uint8_t* st = smem + s * stage_bytes;
@@ -265,15 +289,19 @@ __global__ void __launch_bounds__(lns_threads(TEAMS), 1) ln_stream_kernel(const 
   // team takes row w % 8 of each
   const int nv = D >> 2;  // 4-element vectors per row
   const int team = warp / kLnsRows, wr = warp % kLnsRows;
-  int it = team;
-  for (long long g = blockIdx.x + static_cast<long long>(team) * gridDim.x; g < groups;
-       g += static_cast<long long>(TEAMS) * gridDim.x, it += TEAMS) {
+  for (int it = team; it < n_mine; it += TEAMS) {
+    const long long g = group_at(it);
     const int s = it % p.stages;
     const long long row = g * kLnsRows + wr;
     const bool have = row < p.M;
     bool row_valid = true;
     if (p.valid != nullptr && have) row_valid = p.valid[row] != 0;
-    if (!mbar_wait(&full[s], (it / p.stages) & 1, p.status, kDevTimeoutEpilogue)) break;
+    // ready mode: a stage can stay empty for as long as the producer's count
+    // wait (bounded by kWaitLimitNs itself), so the consumers wait twice that
+    // and leave as soon as the producer records why it gave up
+    if (!mbar_wait_ns(&full[s], (it / p.stages) & 1, p.status, kDevTimeoutEpilogue,
+                      p.ready != nullptr ? 2 * kWaitLimitNs : kWaitLimitNs))
+      break;
     if (have) {
       const uint8_t* xrow = smem + s * stage_bytes + static_cast<long long>(wr) * D * XS;
       const uint2* ds = reinterpret_cast<const uint2*>(smem + s * stage_bytes + x_bytes) + static_cast<long long>(wr) * nv;
@@ -362,8 +390,9 @@ __global__ void __launch_bounds__(lns_threads(TEAMS), 1) ln_stream_kernel(const 
 template <int XT>
 static int ln_launch(const void* x, const void* delta, const float* w, const float* b, float eps,
                      const uint8_t* valid, long long M, int D, int flags, void* x_out, void* normed,
-                     cudaStream_t stream) {
+                     cudaStream_t stream, int* ready = nullptr) {
   constexpr int XS = XT == kLnF32 ? 4 : 2;
+  if (ready != nullptr && D > 2048) return set_error(TF_ERR_SHAPE, "ln_ready: D=%d above 2048", D);
   if (D <= 2048) {
     LnsParams lp;
     lp.x = x;
@@ -379,6 +408,7 @@ static int ln_launch(const void* x, const void* delta, const float* w, const flo
     lp.eps = eps;
     lp.status = device_status_ptr();
     if (lp.status == nullptr) return last_error_code();
+    lp.ready = ready;
     const int stage_bytes = kLnsRows * D * (XS + (delta != nullptr ? 2 : 0));
     // teams and stages (a multiple of the team count, see the kernel's
     // stage-ownership note), best measured at the c3/c4 shapes: three teams
@@ -477,6 +507,30 @@ int ln_residual(const void* x, const void* delta, const float* w, const float* b
   if (flags & TF_LN_X_F16)
     return ln_launch<kLnF16>(x, delta, w, b, eps, valid, M, D, flags, x_out, normed, stream);
   return ln_launch<kLnF32>(x, delta, w, b, eps, valid, M, D, flags, x_out, normed, stream);
+}
+
+int ln_ready(const void* x, const float* w, const float* b, float eps, const uint8_t* valid, long long M, int D,
+             int flags, void* normed, int* ready, cudaStream_t stream) {
+  if (M <= 0) return TF_OK;
+  if (D <= 0 || D % 8 != 0 || D > 2048)
+    return set_error(TF_ERR_SHAPE, "ln_ready: D=%d must be a positive multiple of 8, <= 2048", D);
+  if (flags & ~(TF_LN_MASK_OUT | TF_LN_OUT_F32 | TF_LN_X_F16 | TF_LN_X_BF16))
+    return set_error(TF_ERR_SHAPE, "ln_ready: flags %d (only MASK_OUT, OUT_F32, X_F16, X_BF16)", flags);
+  if ((flags & TF_LN_X_F16) && (flags & TF_LN_X_BF16))
+    return set_error(TF_ERR_SHAPE, "ln_ready: TF_LN_X_F16 and TF_LN_X_BF16 together");
+  if (x == nullptr || w == nullptr || b == nullptr || normed == nullptr || ready == nullptr)
+    return set_error(TF_ERR_SHAPE, "ln_ready: x, w, b, normed and ready are required");
+  if (!aligned16(x) || !aligned16(w) || !aligned16(b) || !aligned16(normed) ||
+      reinterpret_cast<uintptr_t>(ready) % 4 != 0)
+    return set_error(TF_ERR_ALIGN, "ln_ready: x, w, b, normed 16-byte aligned, ready 4-byte aligned");
+  if ((flags & TF_LN_MASK_OUT) && valid == nullptr)
+    return set_error(TF_ERR_SHAPE, "ln_ready: TF_LN_MASK_OUT without a valid-token mask");
+  if (!(flags & TF_LN_MASK_OUT)) valid = nullptr;
+  if (flags & TF_LN_X_BF16)
+    return ln_launch<kLnBF16>(x, nullptr, w, b, eps, valid, M, D, flags, nullptr, normed, stream, ready);
+  if (flags & TF_LN_X_F16)
+    return ln_launch<kLnF16>(x, nullptr, w, b, eps, valid, M, D, flags, nullptr, normed, stream, ready);
+  return ln_launch<kLnF32>(x, nullptr, w, b, eps, valid, M, D, flags, nullptr, normed, stream, ready);
 }
 
 }  // namespace tfb

@@ -89,6 +89,57 @@ def ln_residual(x: torch.Tensor, delta: Optional[torch.Tensor], weight: torch.Te
     return (x_out if write_x else x), normed
 
 
+def ready_counters(rows: int, device) -> torch.Tensor:
+    """Zeroed per-8-row-group counters for a linear_residual / ln_ready pair."""
+    return torch.zeros((rows + 7) // 8, dtype=torch.int32, device=device)
+
+
+def _check_ready(ready: torch.Tensor, rows: int, name: str) -> None:
+    if ready.dtype != torch.int32 or not ready.is_contiguous() or ready.numel() < (rows + 7) // 8:
+        raise ValueError(f"{name}: ready must be contiguous int32 with ceil(rows / 8) entries")
+
+
+def ln_ready(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, eps: float, ready: torch.Tensor,
+             valid: Optional[torch.Tensor] = None, *, mask_out: bool = False,
+             out_dtype: Optional[torch.dtype] = None, normed: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """LayerNorm of x while the linear_residual(..., ready=ready) launched just
+    before it on this stream is still storing x (tf_ln_ready): each 8-row group
+    is normalised once its count reaches D, and its count is reset to 0.
+    normed = mask_out(LayerNorm(x) * weight + bias), fp16 (fp32 x) or x's type
+    (half x) unless out_dtype is fp32. D <= 2048."""
+    _need_cuda("ln_ready", x, weight, bias, ready, valid, normed)
+    if x.dtype not in (torch.float32,) + HALF_TYPES or not x.is_contiguous():
+        raise ValueError("ln_ready: x must be contiguous fp32, fp16 or bf16")
+    if weight.dtype != torch.float32 or bias.dtype != torch.float32:
+        raise ValueError("ln_ready: weight and bias must be fp32")
+    half = x.dtype in HALF_TYPES
+    d = x.shape[-1]
+    m = x.numel() // d
+    _check_ready(ready, m, "ln_ready")
+    flags = 0
+    if mask_out:
+        if valid is None or valid.numel() != m or valid.dtype not in (torch.bool, torch.uint8):
+            raise ValueError("ln_ready: mask_out needs a bool/uint8 mask with one entry per row")
+        valid = valid.contiguous()
+        flags |= _abi.TF_LN_MASK_OUT
+    if x.dtype == torch.float16:
+        flags |= _abi.TF_LN_X_F16
+    elif x.dtype == torch.bfloat16:
+        flags |= _abi.TF_LN_X_BF16
+    io_dtype = x.dtype if half else torch.float16
+    if out_dtype is None:
+        out_dtype = io_dtype
+    if out_dtype == torch.float32:
+        flags |= _abi.TF_LN_OUT_F32
+    elif out_dtype != io_dtype:
+        raise ValueError(f"ln_ready: out_dtype must be {io_dtype} or fp32")
+    if normed is None:
+        normed = torch.empty(x.shape, dtype=out_dtype, device=x.device)
+    _abi.call("tf_ln_ready", _ptr(x), _ptr(weight), _ptr(bias), float(eps), _ptr(valid) if mask_out else None,
+              m, d, flags, _ptr(normed), _ptr(ready), _stream())
+    return normed
+
+
 def _gemm_operands(name, a, w, b, w_split):
     _need_cuda(name, a, w, b)
     if a.dtype not in HALF_TYPES or w.dtype != a.dtype:
@@ -177,13 +228,16 @@ def linear_residual(a: torch.Tensor, w: torch.Tensor, b: torch.Tensor, x_in: tor
                     x_out: Optional[torch.Tensor] = None, valid: Optional[torch.Tensor] = None, *,
                     mask_delta: bool = False, mask_x: bool = False, w_split: bool = False, tile_n: int = 0,
                     pair: int = 0, splits: Optional[int] = None,
-                    workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
+                    workspace: Optional[torch.Tensor] = None, ready: Optional[torch.Tensor] = None) -> torch.Tensor:
     """GEMM closing a residual connection (tf_gemm_residual):
     x_out = mask_x(x_in + mask_delta(a @ w.T + b)). x_in/x_out [..., N]
     contiguous (x_out may be x_in), fp32, or a's type for a half-precision
     model (then both the Linear's output and the sum are rounded to it, as the
     eager model stores them); valid bool/uint8 [rows] for the masks.
-    splits (0 = automatic) selects tf_gemm_residual_splitk."""
+    splits (0 = automatic) selects tf_gemm_residual_splitk. ready (int32
+    [ceil(rows / 8)], zero, from ready_counters) selects
+    tf_gemm_residual_ready: the epilogue counts the stored columns per 8-row
+    group for an ln_ready launched right after it."""
     a2, n, k = _gemm_operands("linear_residual", a, w, b, w_split)
     _need_cuda("linear_residual", x_in, x_out, valid)
     if x_in.dtype not in (torch.float32, a.dtype) or not x_in.is_contiguous() or x_in.shape[-1] != n:
@@ -204,6 +258,15 @@ def linear_residual(a: torch.Tensor, w: torch.Tensor, b: torch.Tensor, x_in: tor
         _abi.TF_RES_BF16 if a.dtype == torch.bfloat16 else 0)
     if valid is not None and not valid.is_contiguous():
         valid = valid.contiguous()
+    if ready is not None:
+        _need_cuda("linear_residual", ready)
+        if splits is not None or tile_n or pair:
+            raise ValueError("linear_residual: ready counters take the automatic, unsplit tiling")
+        _check_ready(ready, m, "linear_residual")
+        _abi.call("tf_gemm_residual_ready", _ptr(a2), a2.stride(0), _ptr(w), w.stride(0), _ptr(b), _ptr(x_in),
+                  _ptr(x_out), n, _ptr(valid) if mode else None, mode | opts, m, n, k, 1 if w_split else 0,
+                  _ptr(ready), _stream())
+        return x_out
     if splits is not None:
         if w_split:
             raise ValueError("linear_residual: split-K does not take split weights")

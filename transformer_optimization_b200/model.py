@@ -228,6 +228,10 @@ class UserOptimizedTransformer(BaselineTransformer):
         # 173); False keeps fp32 scores (closer to the fp32 model, further
         # from eager T)
         self.round_half_scores = True
+        # unsplit residual projections: the LayerNorm after each one starts on
+        # the rows the GEMM has finished while its last wave still runs
+        # (tf_gemm_residual_ready + tf_ln_ready); False runs it after the GEMM
+        self.overlap_ln = True
 
     def _model_dtype(self) -> torch.dtype:
         return self.final_norm.weight.dtype
@@ -322,6 +326,12 @@ class UserOptimizedTransformer(BaselineTransformer):
                 # through their cache entries (_GraphCacheEntry.workspace)
                 ws = self._splitk_ws = torch.empty(need, dtype=torch.uint8, device=dev)
         self._last_ws_used = ws is not None
+        # per-8-row-group counters for the GEMM -> LayerNorm pairs that overlap
+        # (zeroed here every forward, and by each LayerNorm as it consumes them)
+        lno = self.overlap_ln and d <= 2048
+        ready_o = lno and sk_o is None
+        ready_2 = lno and sk_2 is None and chunk is None
+        ready = kernels.ready_counters(m, dev) if (ready_o or ready_2) else None
 
         # With split-K residual projections (few rows), their reduce kernel also
         # runs the LayerNorm that follows (the next layer's norm1, or the final
@@ -342,6 +352,10 @@ class UserOptimizedTransformer(BaselineTransformer):
                 cur, _ = kernels.linear_residual_ln(ctx, w.wo, w.bo, cur, x_res, vflat, w.n2w, w.n2b,
                                                     blk.norm2.eps, mask_delta=mask_active, normed=normed,
                                                     splits=sk_o, workspace=ws)
+            elif ready_o:
+                cur = kernels.linear_residual(ctx, w.wo, w.bo, cur, x_res, vflat, mask_delta=mask_active,
+                                              ready=ready)
+                kernels.ln_ready(cur, w.n2w, w.n2b, blk.norm2.eps, ready, normed=normed)
             else:
                 cur = kernels.linear_residual(ctx, w.wo, w.bo, cur, x_res, vflat, mask_delta=mask_active)
                 kernels.ln_residual(cur, None, w.n2w, w.n2b, blk.norm2.eps, normed=normed)
@@ -359,7 +373,18 @@ class UserOptimizedTransformer(BaselineTransformer):
                 continue
             kernels.linear(normed, w.w1, w.b1, gelu=True, out=hidden, splits=sk_1, workspace=ws,
                            round_gelu_input=half)
-            if sk_2 is None:
+            if sk_2 is None and ready_2:
+                cur = kernels.linear_residual(hidden, w.w2, w.b2, cur, x_res, vflat, mask_x=mask_active,
+                                              w_split=w.split_w2, ready=ready)
+                if li + 1 < n_layers:
+                    wn, nxt = wts[li + 1], self.layers[li + 1]
+                    kernels.ln_ready(cur, wn.n1w, wn.n1b, nxt.norm1.eps, ready, normed=normed)
+                    normed_ready = True
+                else:
+                    fw, fb = self._final_ln
+                    out = kernels.ln_ready(cur, fw, fb, self.final_norm.eps, ready, vflat, mask_out=mask_active,
+                                           out_dtype=x.dtype)
+            elif sk_2 is None:
                 kernels.linear_residual(hidden, w.w2, w.b2, cur, x_res, vflat, mask_x=mask_active,
                                         w_split=w.split_w2)
                 normed_ready = False
@@ -435,7 +460,7 @@ class UserOptimizedTransformer(BaselineTransformer):
         if not self.use_cuda_graphs or not self._graph_memory_safe(x):
             return self._forward_core(x, valid_token_mask, mask_active)
         key = (tuple(x.shape), x.dtype, x.device, cfg.causal, mask_kind, self._split_ffn_out(),
-               self.ffn_chunk_budget_bytes, self.round_half_scores)
+               self.ffn_chunk_budget_bytes, self.round_half_scores, self.overlap_ln)
         if key in self._graph_unsupported:
             return self._forward_core(x, valid_token_mask, mask_active)
         self._layer_weights()  # may invalidate cached graphs
