@@ -739,26 +739,29 @@ int gemm_f16(const GemmCall& g, cudaStream_t stream) {
   const int m_tiles = static_cast<int>((M + kGemmBM - 1) / kGemmBM);
   int bn = g.tile_n > 0 ? g.tile_n : choose_bn(m_tiles, static_cast<int>(N), sms);
   if (N % bn != 0) bn = (N % 128 == 0) ? 128 : 64;
-  // 2-SM pairs for grids that fill the device; 1-CTA tiles (more of them)
-  // for small problems
+  // 2-SM pairs once 128-wide pair tiles keep at least 4/5 of the CTA pairs
+  // busy; 1-CTA tiles (more of them) for smaller problems. Measured at the
+  // per-rank c3 shapes of 4 and 8 GPUs: 2048 x 1024 x 4096 with residual
+  // 27.9 -> 26.0 us, 4096 x 1024 x 1024 with residual 19.2 -> 15.1 us.
   bool pair = false;
   if (g.pair == 2) {
     pair = true;
   } else if (g.pair == 0) {
-    const long long pair_tiles = ((M + 255) / 256) * (N / (N % 256 == 0 ? 256 : 128));
-    pair = (N % 128 == 0) && pair_tiles >= sms / 2;
+    const long long pair_tiles128 = ((M + 255) / 256) * (N / 128);
+    pair = (N % 128 == 0) && pair_tiles128 * 5 >= static_cast<long long>(sms / 2) * 4;
   }
   if (pair) {
     if (N % 128 != 0) return set_error(TF_ERR_SHAPE, "gemm: 2-SM tiles need N %% 128 == 0");
     bn = (g.tile_n == 128 || N % 256 != 0) ? 128 : 256;
     if (g.tile_n == 0 && bn == 256) {
       // wave quantisation: prefer 128-wide pair tiles when they fill the
-      // device in fewer weighted waves
+      // device in fewer weighted waves; a 128-wide pair tile costs ~0.82 of
+      // a 256-wide one at K = 1024 (measured: 2048 x 3072 x 1024 takes
+      // 16.6 us in two waves of 256-wide tiles, 20.4 us in three of 128)
       const long long mt = (M + 255) / 256;
       const long long c256 = mt * (N / 256), c128 = mt * (N / 128);
       const int nc = sms / 2;
-      // a 128-wide pair tile costs ~0.6 of a 256-wide one (measured)
-      if (1.25 * double((c128 + nc - 1) / nc) < 2.0 * double((c256 + nc - 1) / nc)) bn = 128;
+      if (0.82 * double((c128 + nc - 1) / nc) < double((c256 + nc - 1) / nc)) bn = 128;
     }
   }
 
