@@ -168,15 +168,18 @@ int tf_gemm_residual(const void* A, int64_t lda, const void* W, int64_t ldw, con
  * tf_gemm_residual_ready is tf_gemm_residual (automatic tiling, x_out
  * contiguous: ldx == N) whose epilogue also adds, for every group of 8 rows,
  * the number of x_out columns it has stored to ready[group]; a group is
- * complete when its count reaches N. ready: int32[ceil(M / 8)] device array,
- * all zero before the call.
+ * complete when its count reaches N. ready: int32[ceil(M / 8) + 2] device
+ * array, all zero before the call (the last two entries are tf_ln_ready's
+ * ticket counters; the GEMM does not touch them).
  * tf_ln_ready is tf_ln_residual without delta (normed = mask_out(LayerNorm(x)
  * * w + b); flags TF_LN_MASK_OUT, TF_LN_OUT_F32, TF_LN_X_F16, TF_LN_X_BF16;
  * D <= 2048) for x being written by a tf_gemm_residual_ready launched just
  * before it on the same stream with the same ready array and N == D: it waits
  * per row group for the count D instead of for the GEMM to finish, so its
- * CTAs run on the SMs the GEMM's last, partial wave leaves idle; each count
- * it consumes is set back to 0, so the array is ready for the next pair.
+ * CTAs run on the SMs the GEMM's last, partial wave leaves idle; groups are
+ * handed out in ascending order from the ticket counters; each count it
+ * consumes and the ticket counters are set back to 0, so the array is ready
+ * for the next pair.
  * After a failed call (or a device timeout) zero the array again. A count
  * that never completes ends in device code 107 after the 2 s wait bound.
  * Replaces out_proj / ffn_out with the residual add and the LayerNorm of the

@@ -173,7 +173,7 @@ def _record_schedule(monkeypatch, cfg, m_rows, chunk_budget=None, overlap_ln=Tru
     monkeypatch.setattr(K, "linear_residual_ln",
                         rec("res_ln", lambda a, w, b, x_in, x_out, *r, **kw: (x_out, torch.zeros(1))))
     monkeypatch.setattr(K, "ln_ready", rec("ln_ready", lambda x, *a, **kw: torch.zeros(1)))
-    monkeypatch.setattr(K, "ready_counters", lambda rows, dev: torch.zeros((rows + 7) // 8, dtype=torch.int32))
+    monkeypatch.setattr(K, "ready_counters", lambda rows, dev: torch.zeros((rows + 7) // 8 + 2, dtype=torch.int32))
     model = UserOptimizedTransformer(cfg)
     model.ffn_chunk_budget_bytes = chunk_budget
     model.overlap_ln = overlap_ln
@@ -203,7 +203,7 @@ def test_forward_schedule_many_rows(monkeypatch):
     assert names == ["ln"] + ["linear", "flash", "res", "ln_ready", "linear", "res", "ln_ready"] * cfg.num_layers
     assert all(kw.get("splits") is None for n, kw in calls if n == "linear")
     readies = [kw["ready"] for n, kw in calls if n == "res"]
-    assert all(r is readies[0] and r.numel() == 8 * 2048 // 8 for r in readies)
+    assert all(r is readies[0] and r.numel() == 8 * 2048 // 8 + 2 for r in readies)
     assert calls[-1][1]["out_dtype"] == torch.float32 and calls[-1][1]["mask_out"] is False
 
 

@@ -103,7 +103,8 @@ def test_ready_count_above_target_is_refused(K):
     m, n = 256, 1024
     x = torch.randn(m, n, device="cuda")
     lnw, lnb = torch.ones(n, device="cuda"), torch.zeros(n, device="cuda")
-    ready = torch.full(((m + 7) // 8,), n + 32, dtype=torch.int32, device="cuda")
+    ready = K.ready_counters(m, x.device)
+    ready[:(m + 7) // 8] = n + 32  # group counts above the row width; ticket counters zero
     K.ln_ready(x, lnw, lnb, 1e-5, ready)
     assert _abi.device_status() == 107
     # the device stays usable

@@ -30,9 +30,12 @@
 // stored columns of every 8-row group; this kernel does not wait for the GEMM
 // grid to finish (no griddepcontrol.wait) but, per group, for the group's
 // count to reach D, then copies it and zeroes the count for the next site.
-// Each CTA takes a contiguous range of groups, so the CTAs that start first
-// (on the SMs the GEMM's last, partial wave leaves idle) take the rows the
-// GEMM finished first, and the LayerNorm runs under the GEMM's tail.
+// The groups are handed out in ascending order from a ticket counter (two
+// ints after the group counts), one at a time per CTA and only after the
+// CTA's previous group was complete: the CTAs that start first (on the SMs
+// the GEMM's last, partial wave leaves idle) take the rows the GEMM finished
+// first, and once the GEMM ends every CTA shares what is left. The last CTA
+// to run out of tickets zeroes the ticket counters.
 #include "common.cuh"
 #include "launch.h"
 
@@ -229,6 +232,7 @@ __global__ void __launch_bounds__(lns_threads(TEAMS), 1) ln_stream_kernel(const 
   float* b_s = w_s + D;
   uint64_t* full = reinterpret_cast<uint64_t*>(b_s + D);
   uint64_t* empty = full + kLnsMaxStages;
+  int* stage_group = reinterpret_cast<int*>(empty + kLnsMaxStages);  // ready mode: group in a stage, -1 = none left
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long long groups = (p.M + kLnsRows - 1) / kLnsRows;
   if (p.stages % TEAMS != 0 || p.stages > kLnsMaxStages) {  // host invariant; refuse rather than race
@@ -246,13 +250,10 @@ __global__ void __launch_bounds__(lns_threads(TEAMS), 1) ln_stream_kernel(const 
   // `normed`, which no kernel still running reads
   if (p.ready == nullptr) pdl_wait();
   pdl_trigger();
-  // this CTA's groups: strided over the grid, or (ready mode) one contiguous
-  // range, its it-th group being group_at(it)
-  const bool contiguous = p.ready != nullptr;
-  const long long g_lo = contiguous ? groups * blockIdx.x / gridDim.x : blockIdx.x;
-  const long long n_mine = contiguous ? groups * (blockIdx.x + 1) / gridDim.x - g_lo
-                                      : (groups - blockIdx.x + gridDim.x - 1) / gridDim.x;
-  auto group_at = [&](long long it) { return contiguous ? g_lo + it : g_lo + it * gridDim.x; };
+  // this CTA's groups: strided over the grid (its it-th group is
+  // blockIdx.x + it * gridDim.x), or (ready mode) drawn from the ticket counter
+  const bool dynamic = p.ready != nullptr;
+  const long long n_mine = dynamic ? 0x7fffffff : (groups - blockIdx.x + gridDim.x - 1) / gridDim.x;
   for (int i = threadIdx.x; i < (D >> 2); i += blockDim.x) {
     reinterpret_cast<float4*>(w_s)[i] = __ldg(reinterpret_cast<const float4*>(p.w) + i);
     reinterpret_cast<float4*>(b_s)[i] = __ldg(reinterpret_cast<const float4*>(p.b) + i);
@@ -262,12 +263,19 @@ __global__ void __launch_bounds__(lns_threads(TEAMS), 1) ln_stream_kernel(const 
   if (warp == kLnsRows * TEAMS) {
     // ---------------- producer ----------------
     if (lane == 0) {
-      for (int it = 0; it < n_mine; ++it) {
-        const long long g = group_at(it);
+      int* ticket = dynamic ? p.ready + groups : nullptr;  // next group to hand out
+      int* done = ticket + 1;                              // CTAs out of tickets
+      bool ok = true;
+      int it = 0;
+      for (; it < n_mine; ++it) {
         const int s = it % p.stages;
-        if (!mbar_wait(&empty[s], ((it / p.stages) & 1) ^ 1, p.status, kDevTimeoutProducer)) break;
-        if (p.ready != nullptr) {
-          if (!wait_ready(p.ready + g, D, p.status)) break;
+        if (!(ok = mbar_wait(&empty[s], ((it / p.stages) & 1) ^ 1, p.status, kDevTimeoutProducer))) break;
+        long long g = blockIdx.x + static_cast<long long>(it) * gridDim.x;
+        if (dynamic) {
+          g = atomicAdd(ticket, 1);
+          if (g >= groups) break;  // stage s (already free) takes the first stop below
+          stage_group[s] = static_cast<int>(g);
+          if (!(ok = wait_ready(p.ready + g, D, p.status))) break;
           fence_proxy_async_global();
           p.ready[g] = 0;  // consumed; the next site's GEMM starts after this grid ends
         }
@@ -280,6 +288,21 @@ __global__ void __launch_bounds__(lns_threads(TEAMS), 1) ln_stream_kernel(const 
         bulk_load_1d(st, static_cast<const uint8_t*>(p.x) + r0 * D * XS, xb, &full[s]);
         if (has_delta) bulk_load_1d(st + x_bytes, p.delta + r0 * D, db, &full[s]);
       }
+      if (dynamic && ok) {
+        // one stop per team: the stages of this CTA's next TEAMS groups
+        for (int k = 0; k < TEAMS && ok; ++k, ++it) {
+          const int s = it % p.stages;
+          if (k > 0 && !(ok = mbar_wait(&empty[s], ((it / p.stages) & 1) ^ 1, p.status, kDevTimeoutProducer)))
+            break;
+          stage_group[s] = -1;
+          mbar_arrive(&full[s]);
+        }
+        // no CTA draws a ticket after the last one has run out: reset both
+        if (atomicAdd(done, 1) == static_cast<int>(gridDim.x) - 1) {
+          *ticket = 0;
+          *done = 0;
+        }
+      }
     }
     return;
   }
@@ -290,18 +313,24 @@ __global__ void __launch_bounds__(lns_threads(TEAMS), 1) ln_stream_kernel(const 
   const int nv = D >> 2;  // 4-element vectors per row
   const int team = warp / kLnsRows, wr = warp % kLnsRows;
   for (int it = team; it < n_mine; it += TEAMS) {
-    const long long g = group_at(it);
     const int s = it % p.stages;
-    const long long row = g * kLnsRows + wr;
-    const bool have = row < p.M;
+    long long g = blockIdx.x + static_cast<long long>(it) * gridDim.x;
+    long long row = g * kLnsRows + wr;
     bool row_valid = true;
-    if (p.valid != nullptr && have) row_valid = p.valid[row] != 0;
+    if (!dynamic && p.valid != nullptr && row < p.M) row_valid = p.valid[row] != 0;  // ahead of the wait
     // ready mode: a stage can stay empty for as long as the producer's count
     // wait (bounded by kWaitLimitNs itself), so the consumers wait twice that
     // and leave as soon as the producer records why it gave up
     if (!mbar_wait_ns(&full[s], (it / p.stages) & 1, p.status, kDevTimeoutEpilogue,
-                      p.ready != nullptr ? 2 * kWaitLimitNs : kWaitLimitNs))
+                      dynamic ? 2 * kWaitLimitNs : kWaitLimitNs))
       break;
+    if (dynamic) {
+      g = stage_group[s];
+      if (g < 0) break;  // no group left for this team
+      row = g * kLnsRows + wr;
+      if (p.valid != nullptr && row < p.M) row_valid = p.valid[row] != 0;
+    }
+    const bool have = row < p.M;
     if (have) {
       const uint8_t* xrow = smem + s * stage_bytes + static_cast<long long>(wr) * D * XS;
       const uint2* ds = reinterpret_cast<const uint2*>(smem + s * stage_bytes + x_bytes) + static_cast<long long>(wr) * nv;
@@ -420,7 +449,7 @@ static int ln_launch(const void* x, const void* delta, const float* w, const flo
     const int stages = (fit / teams) * teams;
     if (stages < teams) return set_error(TF_ERR_SHAPE, "ln_residual: D=%d too wide for the streaming kernel", D);
     lp.stages = stages;
-    const int smem = stages * stage_bytes + 8 * D + 2 * kLnsMaxStages * 8 + 128;
+    const int smem = stages * stage_bytes + 8 * D + 2 * kLnsMaxStages * 8 + kLnsMaxStages * 4 + 128;
     const long long groups = (M + kLnsRows - 1) / kLnsRows;
     const long long grid = groups < device_sm_count() ? groups : device_sm_count();
     const int nv = (D / 4 + 31) / 32;
@@ -432,7 +461,7 @@ static int ln_launch(const void* x, const void* delta, const float* w, const flo
     if (!attr_done[dev & 63]) {                                                                     \
       cudaError_t ea = cudaFuncSetAttribute(ln_stream_kernel<N, T, XT>,                             \
                                             cudaFuncAttributeMaxDynamicSharedMemorySize,            \
-                                            kLnsSmemBudget + 8 * 2048 + 2 * kLnsMaxStages * 8 + 128); \
+                                            kLnsSmemBudget + 8 * 2048 + 2 * kLnsMaxStages * 8 + kLnsMaxStages * 4 + 128); \
       if (ea != cudaSuccess)                                                                        \
         return set_error(TF_ERR_LAUNCH, "cudaFuncSetAttribute(ln): %s", cudaGetErrorString(ea));    \
       attr_done[dev & 63] = true;                                                                   \

@@ -90,13 +90,14 @@ def ln_residual(x: torch.Tensor, delta: Optional[torch.Tensor], weight: torch.Te
 
 
 def ready_counters(rows: int, device) -> torch.Tensor:
-    """Zeroed per-8-row-group counters for a linear_residual / ln_ready pair."""
-    return torch.zeros((rows + 7) // 8, dtype=torch.int32, device=device)
+    """Zeroed counters for a linear_residual / ln_ready pair: one per 8-row
+    group, then the LayerNorm's two ticket counters."""
+    return torch.zeros((rows + 7) // 8 + 2, dtype=torch.int32, device=device)
 
 
 def _check_ready(ready: torch.Tensor, rows: int, name: str) -> None:
-    if ready.dtype != torch.int32 or not ready.is_contiguous() or ready.numel() < (rows + 7) // 8:
-        raise ValueError(f"{name}: ready must be contiguous int32 with ceil(rows / 8) entries")
+    if ready.dtype != torch.int32 or not ready.is_contiguous() or ready.numel() < (rows + 7) // 8 + 2:
+        raise ValueError(f"{name}: ready must be contiguous int32 with ceil(rows / 8) + 2 entries")
 
 
 def ln_ready(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, eps: float, ready: torch.Tensor,
@@ -235,7 +236,7 @@ def linear_residual(a: torch.Tensor, w: torch.Tensor, b: torch.Tensor, x_in: tor
     model (then both the Linear's output and the sum are rounded to it, as the
     eager model stores them); valid bool/uint8 [rows] for the masks.
     splits (0 = automatic) selects tf_gemm_residual_splitk. ready (int32
-    [ceil(rows / 8)], zero, from ready_counters) selects
+    [ceil(rows / 8) + 2], zero, from ready_counters) selects
     tf_gemm_residual_ready: the epilogue counts the stored columns per 8-row
     group for an ln_ready launched right after it."""
     a2, n, k = _gemm_operands("linear_residual", a, w, b, w_split)
