@@ -436,8 +436,9 @@ def test_flash_fully_masked_rows(K):
     assert torch.all(torch.isneginf(lse))
 
 
-def test_attn_merge(K):
-    b, s, h, hd = 2, 100, 4, 64
+@pytest.mark.parametrize("b,s,h,hd", [(2, 100, 4, 64), (1, 300, 16, 64), (2, 77, 8, 128), (1, 50, 40, 32)])
+def test_attn_merge(K, b, s, h, hd):
+    """Row-per-warp form (heads <= 32) and the per-head form (40 heads)."""
     g = torch.Generator().manual_seed(3)
     oa = torch.randn(b, s, h * hd, generator=g)
     ob = torch.randn(b, s, h * hd, generator=g)

@@ -680,6 +680,56 @@ __global__ void attn_merge_kernel(float* __restrict__ o_acc, float* __restrict__
   if (lane == 0) lse_acc[li] = L;
 }
 
+// The same merge with one warp per (batch, token row) covering all heads:
+// lanes 0..heads-1 compute their head's weights once, and the row's
+// heads*hd values move as float4 with their head's weights taken from that
+// lane (heads <= 32, hd % 4 == 0, 16-byte aligned rows). Per element the
+// arithmetic is the one above.
+__global__ void attn_merge_rows_kernel(float* __restrict__ o_acc, float* __restrict__ lse_acc,
+                                       const float* __restrict__ o_part, const float* __restrict__ lse_part,
+                                       long long ld, long long bs, __half* __restrict__ out16, long long ld16,
+                                       long long bs16, int heads, int seq_q, int hd, long long rows) {
+  pdl_wait();
+  pdl_trigger();
+  const long long gw = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (gw >= rows) return;  // whole warps leave together
+  const int b = static_cast<int>(gw / seq_q);
+  const int i = static_cast<int>(gw % seq_q);
+  float wa = 0.f, wb = 0.f;
+  if (lane < heads) {
+    const long long li = (static_cast<long long>(b) * heads + lane) * seq_q + i;
+    const float la = lse_acc[li], lb = lse_part[li];
+    const float mx = fmaxf(la, lb);
+    const float L = mx == -INFINITY ? -INFINITY : mx + log1pf(__expf(-fabsf(la - lb)));
+    wa = la == -INFINITY ? 0.f : __expf(la - L);
+    wb = lb == -INFINITY ? 0.f : __expf(lb - L);
+    lse_acc[li] = L;
+  }
+  float4* pa = reinterpret_cast<float4*>(o_acc + static_cast<long long>(b) * bs + static_cast<long long>(i) * ld);
+  const float4* pb =
+      reinterpret_cast<const float4*>(o_part + static_cast<long long>(b) * bs + static_cast<long long>(i) * ld);
+  uint2* p16 = out16 == nullptr ? nullptr
+                                : reinterpret_cast<uint2*>(out16 + static_cast<long long>(b) * bs16 +
+                                                           static_cast<long long>(i) * ld16);
+  const int nv = heads * hd / 4;
+  for (int base = 0; base < nv; base += 32) {
+    const int q = base + lane;
+    const int h = q < nv ? (4 * q) / hd : 0;
+    const float ca = __shfl_sync(0xffffffffu, wa, h);
+    const float cb = __shfl_sync(0xffffffffu, wb, h);
+    if (q < nv) {
+      const float4 x = pa[q], y = __ldcs(pb + q);
+      const float4 v = make_float4(x.x * ca + y.x * cb, x.y * ca + y.y * cb, x.z * ca + y.z * cb, x.w * ca + y.w * cb);
+      pa[q] = v;
+      if (p16 != nullptr) {
+        const __half2 h0 = __floats2half2_rn(v.x, v.y), h1 = __floats2half2_rn(v.z, v.w);
+        __stcs(p16 + q, make_uint2(*reinterpret_cast<const uint32_t*>(&h0), *reinterpret_cast<const uint32_t*>(&h1)));
+      }
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
@@ -802,6 +852,21 @@ int attn_merge(const MergeArgs& a, cudaStream_t stream) {
   if (a.head_dim <= 0 || a.batch > 65535) return set_error(TF_ERR_SHAPE, "merge: bad sizes");
   if (a.o_acc == nullptr || a.lse_acc == nullptr || a.o_part == nullptr || a.lse_part == nullptr)
     return set_error(TF_ERR_SHAPE, "merge: null operand");
+  const bool rows_form = a.heads <= 32 && a.head_dim % 4 == 0 && a.ld % 4 == 0 && a.bs % 4 == 0 &&
+                         aligned16(a.o_acc) && aligned16(a.o_part) &&
+                         (a.out16 == nullptr ||
+                          (reinterpret_cast<uintptr_t>(a.out16) % 8 == 0 && a.ld16 % 4 == 0 && a.bs16 % 4 == 0));
+  if (rows_form) {
+    const long long rows = a.batch * a.seq_q;
+    const long long blocks = (rows * 32 + 255) / 256;
+    if (blocks > 0x7fffffffll) return set_error(TF_ERR_SHAPE, "merge: too many rows");
+    launch_k(attn_merge_rows_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, stream, a.o_acc, a.lse_acc,
+             a.o_part, a.lse_part, a.ld, a.bs, static_cast<__half*>(a.out16), a.ld16, a.bs16,
+             static_cast<int>(a.heads), static_cast<int>(a.seq_q), static_cast<int>(a.head_dim), rows);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return set_error(TF_ERR_LAUNCH, "merge launch: %s", cudaGetErrorString(e));
+    return TF_OK;
+  }
   const long long warps = a.heads * a.seq_q;
   const long long blocks = (warps * 32 + 255) / 256;
   if (blocks > 0x7fffffffll) return set_error(TF_ERR_SHAPE, "merge: too many rows");
