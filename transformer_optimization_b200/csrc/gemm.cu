@@ -43,6 +43,13 @@ constexpr int kGemmBK = 64;  // one 128-byte swizzle row of fp16
 constexpr int kGemmThreads = 192;
 constexpr int kEpiTileFloats = 32 * 32;  // one warp's epilogue staging tile (32 x 32 fp32)
 constexpr int kMaxSplits = 32;           // split-K: most k ranges per tile
+// k-blocks per stage group: the MMA thread waits once and commits once per
+// group. Every barrier wait and commit of the issuing thread leaves the tensor
+// pipe idle for a while (its MMA queue is shallow); measured on B200 with the
+// c3 forward (alternating on one box, 3 runs each): 1 k-block 7.95 ms, 2
+// k-blocks 7.82 ms (GEMMs 1120 -> 1145 TFLOP/s in the step); 3 k-blocks per
+// group (two groups of the 2-SM kernel's six stages) was slower than 1.
+constexpr int kGemmGroupKb = 2;
 
 struct GemmArgs {
   const float* bias;
@@ -216,7 +223,7 @@ __device__ __forceinline__ void signal_rows(const GemmArgs& p, int row0, int col
   }
 }
 
-template <int BN, int STAGES, int EPI, int DT>
+template <int BN, int STAGES, int EPI, int DT, int KG>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_f16_tcgen05(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      GemmArgs p) {
@@ -270,43 +277,53 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   pdl_wait();
   pdl_trigger();
 
+  // Stages are filled and consumed in groups of KG k-blocks: one `full` wait
+  // and one commit per group (kGemmGroupKb). Group barrier g covers stages
+  // KG*g .. KG*g+KG-1.
+  constexpr int kGroups = STAGES / KG;
+  static_assert(STAGES % KG == 0, "stages are used in groups of KG");
   if (warp == 0) {
     if (lane == 0) {
       // ---------------- TMA producer ----------------
-      int it = 0;
+      int ig = 0;
       bool ok = true;
       for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
         int t, sp, kb_lo, kb_hi;
         unit_range(u, t, sp, kb_lo, kb_hi);
         const int m0 = (t / p.n_tiles) * kGemmBM;
         const int n0 = (t % p.n_tiles) * BN;
-        for (int kb = kb_lo; kb < kb_hi; ++kb, ++it) {
-          const int s = it % STAGES;
-          const uint32_t ph = (it / STAGES) & 1;
-          if (!mbar_wait(&empty[s], ph ^ 1, p.status, kDevTimeoutProducer)) {
+        for (int kg = kb_lo; kg < kb_hi; kg += KG, ++ig) {
+          const int sg = ig % kGroups;
+          const uint32_t ph = (ig / kGroups) & 1;
+          if (!mbar_wait(&empty[sg], ph ^ 1, p.status, kDevTimeoutProducer)) {
             ok = false;
             break;
           }
-          uint8_t* sa = smem + s * L::kStageBytes;
-          mbar_arrive_expect_tx(&full[s], L::kStageBytes);
-          const int akb = kb < a_blocks ? kb : kb - a_blocks;
-          tma_load_2d(sa, &tmA, &full[s], akb * kGemmBK, m0);
-          // W block: columns [kb*64, kb*64+64) of [W_hi | W_lo]; with a
-          // K tail the lo half starts at column K, not at a_blocks*64
-          const int wcol = kb < a_blocks ? kb * kGemmBK : p.K + akb * kGemmBK;
-          tma_load_2d(sa + L::kABytes, &tmB, &full[s], wcol, n0);
+          const int nkb = kb_hi - kg < KG ? kb_hi - kg : KG;
+          mbar_arrive_expect_tx(&full[sg], nkb * L::kStageBytes);
+          for (int j = 0; j < nkb; ++j) {
+            const int kb = kg + j;
+            uint8_t* sa = smem + (KG * sg + j) * L::kStageBytes;
+            const int akb = kb < a_blocks ? kb : kb - a_blocks;
+            tma_load_2d(sa, &tmA, &full[sg], akb * kGemmBK, m0);
+            // W block: columns [kb*64, kb*64+64) of [W_hi | W_lo]; with a
+            // K tail the lo half starts at column K, not at a_blocks*64
+            const int wcol = kb < a_blocks ? kb * kGemmBK : p.K + akb * kGemmBK;
+            tma_load_2d(sa + L::kABytes, &tmB, &full[sg], wcol, n0);
+          }
         }
       }
       // Drain: every load this thread issued must land before the CTA exits.
-      const int first = it > STAGES ? it - STAGES : 0;
-      for (int j = first; j < it; ++j) mbar_wait(&full[j % STAGES], (j / STAGES) & 1, p.status, kDevTimeoutDrain);
+      const int first = ig > kGroups ? ig - kGroups : 0;
+      for (int j = first; j < ig; ++j)
+        mbar_wait(&full[j % kGroups], (j / kGroups) & 1, p.status, kDevTimeoutDrain);
     }
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------- MMA issuer ----------------
       constexpr uint32_t idesc = idesc_16_f32(DT, kGemmBM, BN);
       const uint32_t smem_base = smem_u32(smem);
-      int it = 0;
+      int ig = 0;
       int tc = 0;
       bool ok = true;
       for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x, ++tc) {
@@ -317,23 +334,26 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (!mbar_wait(&tempty[a], aph ^ 1, p.status, kDevTimeoutMma)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + a * BN;
-        for (int kb = kb_lo; kb < kb_hi; ++kb, ++it) {
-          const int s = it % STAGES;
-          const uint32_t ph = (it / STAGES) & 1;
-          if (!mbar_wait(&full[s], ph, p.status, kDevTimeoutMma)) {
+        for (int kg = kb_lo; kg < kb_hi; kg += KG, ++ig) {
+          const int sg = ig % kGroups;
+          const uint32_t ph = (ig / kGroups) & 1;
+          if (!mbar_wait(&full[sg], ph, p.status, kDevTimeoutMma)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t sa = smem_base + s * L::kStageBytes;
-          const uint32_t sb = sa + L::kABytes;
+          const int nkb = kb_hi - kg < KG ? kb_hi - kg : KG;
+          for (int j = 0; j < nkb; ++j) {
+            const uint32_t sa = smem_base + (KG * sg + j) * L::kStageBytes;
+            const uint32_t sb = sa + L::kABytes;
 #pragma unroll
-          for (int k = 0; k < kGemmBK / 16; ++k) {
-            const uint64_t ad = smem_desc_sw128(sa + k * 32, 16, 1024);
-            const uint64_t bd = smem_desc_sw128(sb + k * 32, 16, 1024);
-            umma_f16_ss(d_tmem, ad, bd, idesc, (kb != kb_lo || k != 0) ? 1u : 0u);
+            for (int k = 0; k < kGemmBK / 16; ++k) {
+              const uint64_t ad = smem_desc_sw128(sa + k * 32, 16, 1024);
+              const uint64_t bd = smem_desc_sw128(sb + k * 32, 16, 1024);
+              umma_f16_ss(d_tmem, ad, bd, idesc, (kg != kb_lo || j != 0 || k != 0) ? 1u : 0u);
+            }
           }
-          umma_commit(&empty[s]);
+          umma_commit(&empty[sg]);
         }
         if (ok) umma_commit(&tfull[a]);
       }
@@ -423,7 +443,7 @@ struct Gemm2Smem {
   static constexpr int kAlloc = kBytes + 1024;
 };
 
-template <int BN, int STAGES, int EPI, int DT>
+template <int BN, int STAGES, int EPI, int DT, int KG>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemm2Threads, 1)
     gemm_f16_tcgen05_2sm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                          GemmArgs p) {
@@ -473,42 +493,52 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemm2Threads, 1)
   pdl_wait();
   pdl_trigger();
 
+  // Stages are filled and consumed in groups of KG k-blocks (kGemmGroupKb):
+  // one `full` wait and one commit per group. Group barrier g covers stages
+  // KG*g .. KG*g+KG-1.
+  constexpr int kGroups = STAGES / KG;
+  static_assert(STAGES % KG == 0, "stages are used in groups of KG");
+  const int k_groups = (k_blocks + KG - 1) / KG;
   if (warp == 0) {
     if (lane == 0) {
       // ---------------- TMA producer (both CTAs) ----------------
-      int it = 0;
+      int ig = 0;
       bool ok = true;
       for (int t = cluster_id; t < total_tiles && ok; t += n_clusters) {
         const int m0 = (t / p.n_tiles) * 256 + static_cast<int>(rank) * 128;
         const int n0 = (t % p.n_tiles) * BN + static_cast<int>(rank) * (BN / 2);
-        for (int kb = 0; kb < k_blocks; ++kb, ++it) {
-          const int s = it % STAGES;
-          const uint32_t ph = (it / STAGES) & 1;
-          if (!mbar_wait(&empty[s], ph ^ 1, p.status, kDevTimeoutProducer)) {
+        for (int g = 0; g < k_groups; ++g, ++ig) {
+          const int sg = ig % kGroups;
+          const uint32_t ph = (ig / kGroups) & 1;
+          if (!mbar_wait(&empty[sg], ph ^ 1, p.status, kDevTimeoutProducer)) {
             ok = false;
             break;
           }
-          uint8_t* sa = smem + s * L::kStageBytes;
-          const uint32_t bar = mapa_shared(smem_u32(&full[s]), 0);
-          if (leader) mbar_arrive_expect_tx(&full[s], 2 * L::kStageBytes);
-          const int akb = kb < a_blocks ? kb : kb - a_blocks;
-          const int wcol = kb < a_blocks ? kb * kGemmBK : p.K + akb * kGemmBK;
-          tma_load_2d_pair(sa, &tmA, bar, akb * kGemmBK, m0);
-          tma_load_2d_pair(sa + L::kABytes, &tmB, bar, wcol, n0);
+          const int nkb = k_blocks - KG * g < KG ? k_blocks - KG * g : KG;
+          const uint32_t bar = mapa_shared(smem_u32(&full[sg]), 0);
+          if (leader) mbar_arrive_expect_tx(&full[sg], nkb * 2 * L::kStageBytes);
+          for (int j = 0; j < nkb; ++j) {
+            const int kb = KG * g + j;
+            uint8_t* sa = smem + (KG * sg + j) * L::kStageBytes;
+            const int akb = kb < a_blocks ? kb : kb - a_blocks;
+            const int wcol = kb < a_blocks ? kb * kGemmBK : p.K + akb * kGemmBK;
+            tma_load_2d_pair(sa, &tmA, bar, akb * kGemmBK, m0);
+            tma_load_2d_pair(sa + L::kABytes, &tmB, bar, wcol, n0);
+          }
         }
       }
       // Drain: wait until the MMAs have consumed every stage this CTA loaded
-      // (the commit that frees a stage also proves its loads landed).
-      const int first = it > STAGES ? it - STAGES : 0;
-      for (int j = first; j < it; ++j)
-        mbar_wait(&empty[j % STAGES], ((j / STAGES) & 1), p.status, kDevTimeoutDrain);
+      // (the commit that frees a group also proves its loads landed).
+      const int first = ig > kGroups ? ig - kGroups : 0;
+      for (int j = first; j < ig; ++j)
+        mbar_wait(&empty[j % kGroups], ((j / kGroups) & 1), p.status, kDevTimeoutDrain);
     }
   } else if (warp == 1) {
     if (lane == 0 && leader) {
       // ---------------- MMA issuer (leader) ----------------
       constexpr uint32_t idesc = idesc_16_f32(DT, 256, BN);
       const uint32_t smem_base = smem_u32(smem);
-      int it = 0;
+      int ig = 0;
       int tc = 0;
       bool ok = true;
       for (int t = cluster_id; t < total_tiles && ok; t += n_clusters, ++tc) {
@@ -517,21 +547,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemm2Threads, 1)
         if (!mbar_wait(&tempty[a], aph ^ 1, p.status, kDevTimeoutMma)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + a * BN;
-        for (int kb = 0; kb < k_blocks; ++kb, ++it) {
-          const int s = it % STAGES;
-          const uint32_t ph = (it / STAGES) & 1;
-          if (!mbar_wait(&full[s], ph, p.status, kDevTimeoutMma)) {
+        for (int g = 0; g < k_groups; ++g, ++ig) {
+          const int sg = ig % kGroups;
+          const uint32_t ph = (ig / kGroups) & 1;
+          if (!mbar_wait(&full[sg], ph, p.status, kDevTimeoutMma)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t sa = smem_base + s * L::kStageBytes;
-          const uint32_t sb = sa + L::kABytes;
+          const int nkb = k_blocks - KG * g < KG ? k_blocks - KG * g : KG;
+          for (int j = 0; j < nkb; ++j) {
+            const uint32_t sa = smem_base + (KG * sg + j) * L::kStageBytes;
+            const uint32_t sb = sa + L::kABytes;
 #pragma unroll
-          for (int k = 0; k < kGemmBK / 16; ++k)
-            umma_f16_ss_pair(d_tmem, smem_desc_sw128(sa + k * 32, 16, 1024), smem_desc_sw128(sb + k * 32, 16, 1024),
-                             idesc, (kb | k) != 0 ? 1u : 0u);
-          umma_commit_pair_mc(&empty[s], 0x3);
+            for (int k = 0; k < kGemmBK / 16; ++k)
+              umma_f16_ss_pair(d_tmem, smem_desc_sw128(sa + k * 32, 16, 1024),
+                               smem_desc_sw128(sb + k * 32, 16, 1024), idesc, (g | j | k) != 0 ? 1u : 0u);
+          }
+          umma_commit_pair_mc(&empty[sg], 0x3);
         }
         if (ok) umma_commit_pair_mc(&tfull[a], 0x3);
       }
@@ -607,7 +640,7 @@ template <int BN, int STAGES, int EPI, int DT>
 static int launch_gemm_cfg(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args, int grid,
                            cudaStream_t stream) {
   using L = GemmSmem<BN, STAGES>;
-  auto kern = gemm_f16_tcgen05<BN, STAGES, EPI, DT>;
+  auto kern = gemm_f16_tcgen05<BN, STAGES, EPI, DT, kGemmGroupKb>;
   static bool attr_done[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -625,7 +658,7 @@ template <int BN, int STAGES, int EPI, int DT>
 static int launch_gemm2_cfg(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args, int grid,
                             cudaStream_t stream) {
   using L = Gemm2Smem<BN, STAGES>;
-  auto kern = gemm_f16_tcgen05_2sm<BN, STAGES, EPI, DT>;
+  auto kern = gemm_f16_tcgen05_2sm<BN, STAGES, EPI, DT, kGemmGroupKb>;
   static bool attr_done[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
