@@ -72,7 +72,7 @@ def emit(line: dict) -> None:
 # DRAM bytes (read + write) per projection launch of the c3 forward at one
 # GPU (M = 16384 rows), mean of the four projections of a layer, from one ncu
 # capture of each shape (the capture summaries are kept with the profiles)
-C3_GEMM_DRAM_BYTES_PER_LAUNCH = 150.9e6
+C3_GEMM_DRAM_BYTES_PER_LAUNCH = 153.3e6
 L2_FLUSH_BYTES = 256 << 20
 
 
