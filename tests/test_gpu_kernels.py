@@ -259,6 +259,20 @@ def test_gemm_pair_tiles(K, m, tile_n, gelu):
     assert torch.all(err <= 2e-3 * ref.abs() + 1e-3), f"max err {err.max()}"
 
 
+@pytest.mark.parametrize("k", [64, 320, 960])
+@pytest.mark.parametrize("pair", [1, 2])
+def test_gemm_odd_kblock_groups(K, k, pair):
+    """The main loop consumes stages in groups of two 64-wide k-blocks; an odd
+    count (1, 5, 15 blocks) ends with a group of one, on both kernel forms."""
+    m, n = 1000, 1536
+    a, w, bias = _gemm_inputs(m, k, n, k + pair)
+    w16 = w.half()
+    ref = om.linear_fp16(a, w16, bias, False)
+    out = K.linear(a.cuda(), w16.cuda(), bias.cuda(), tile_n=256 if pair == 2 else 128, pair=pair).float().cpu()
+    err = (out - ref).abs()
+    assert torch.all(err <= 2e-3 * ref.abs() + 1e-3), f"max err {err.max()}"
+
+
 @pytest.mark.parametrize("mode", ["none", "mask_delta", "mask_x"])
 def test_gemm_residual_large(K, mode):
     """Large enough for the automatic choice to take 2-SM tiles."""
