@@ -182,18 +182,14 @@ def _record_schedule(monkeypatch, cfg, m_rows, chunk_budget=None, overlap_ln=Tru
 
 
 def test_forward_schedule_few_rows(monkeypatch):
-    """c2 (64 rows): the projections take the split-K form except QKV (K =
-    512 stays unsplit, no reduce launch) and each residual site runs the
-    following LayerNorm in its reduce kernel (the next layer's norm1, the
-    final norm after the last layer, fp32 out)."""
+    """c2 (64 rows): every projection takes the split-K form and each
+    residual site runs the following LayerNorm in its reduce kernel (the next
+    layer's norm1, the final norm after the last layer, fp32 out)."""
     cfg = NAMED_CONFIGS["c2"]
     calls = _record_schedule(monkeypatch, cfg, 64)
     names = [c[0] for c in calls]
     assert names == ["ln"] + ["linear", "flash", "res_ln", "linear", "res_ln"] * cfg.num_layers
-    lin = [kw for n, kw in calls if n == "linear"]
-    assert all(kw.get("splits") is None for kw in lin[0::2])          # QKV
-    assert all(kw.get("splits") == 0 for kw in lin[1::2])             # FFN-in
-    assert all(kw.get("splits") == 0 for n, kw in calls if n == "res_ln")
+    assert all(kw.get("splits") == 0 for n, kw in calls if n in ("linear", "res_ln"))
     assert calls[-1][1]["out_dtype"] == torch.float32 and calls[-1][1]["mask_out"] is False
 
 

@@ -314,11 +314,7 @@ class UserOptimizedTransformer(BaselineTransformer):
         # split-K (fp32 partials in a workspace) for the projections of
         # few-row inputs, where 128-row tiles would leave most SMs idle
         sms = props.multi_processor_count
-        # the QKV projection stays unsplit up to K = 512: its reduce launch then
-        # goes away, and the unsplit GEMM is as fast (c1 0.0668 -> 0.0650 ms,
-        # c2 0.1820 -> 0.1815 ms; FFN-in unsplit is slower, 0.182 -> 0.190 ms)
-        sk_qkv = _splitk(m, 3 * d, d, sms) if d > 512 else None
-        sk_o, sk_1 = _splitk(m, d, d, sms), _splitk(m, f, d, sms)
+        sk_qkv, sk_o, sk_1 = _splitk(m, 3 * d, d, sms), _splitk(m, d, d, sms), _splitk(m, f, d, sms)
         sk_2 = None if wts[0].split_w2 else _splitk(m, d, f, sms)
         ws = None
         if any(v is not None for v in (sk_qkv, sk_o, sk_1, sk_2)):
