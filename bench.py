@@ -69,6 +69,8 @@ def emit(line: dict) -> None:
     out = _JSON_OUT if _JSON_OUT is not None else sys.stdout
     out.write(json.dumps(line) + "\n")
     out.flush()
+
+
 # DRAM bytes (read + write) per projection launch of the c3 forward at one
 # GPU (M = 16384 rows), mean of the four projections of a layer, from one ncu
 # capture of each shape (the capture summaries are kept with the profiles)
