@@ -3,6 +3,7 @@
     python -m transformer_optimization_b200.microbench gemm  M N K [--gelu] [--tile-n T]
     python -m transformer_optimization_b200.microbench flash B H S HD [--causal]
     python -m transformer_optimization_b200.microbench ln    M D
+    python -m transformer_optimization_b200.microbench merge B S H HD
 
 Prints one line: kernel, shape, mean time per launch (ms) and the achieved
 rate against its roofline unit (TFLOP/s for GEMM/attention, GB/s for
@@ -53,7 +54,7 @@ def _time(fn, warmup, iters, min_warm_s=0.3, min_time_s=0.2):
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("kernel", choices=("gemm", "gemm_res", "flash", "ln"))
+    ap.add_argument("kernel", choices=("gemm", "gemm_res", "flash", "ln", "merge"))
     ap.add_argument("dims", type=int, nargs="+")
     ap.add_argument("--gelu", action="store_true")
     ap.add_argument("--causal", action="store_true")
@@ -100,6 +101,19 @@ def main(argv=None):
         flops = 4.0 * bsz * s * s * d * (0.5 if a.causal else 1.0)
         print(f"flash B={bsz} H={h} S={s} hd={hd} causal={a.causal}: {ms:.4f} ms  "
               f"{flops / (ms / 1e3) / 1e12:.1f} TFLOP/s")
+    elif a.kernel == "merge":
+        # one ring step's combine (context parallelism): fp32 accumulator and
+        # partial [B, S, H*hd] with their [B, H, S] log-sum-exps, fp16 copy out
+        bsz, s, h, hd = a.dims
+        d = h * hd
+        o_acc = torch.randn(bsz, s, d, device=dev)
+        o_part = torch.randn(bsz, s, d, device=dev)
+        lse_acc = torch.randn(bsz, h, s, device=dev)
+        lse_part = torch.randn(bsz, h, s, device=dev)
+        out16 = torch.empty(bsz, s, d, device=dev, dtype=torch.float16)
+        ms = T(lambda: K.attn_merge(o_acc, lse_acc, o_part, lse_part, h, out16=out16))
+        nbytes = bsz * s * d * (4 + 4 + 4 + 2) + bsz * h * s * 4 * 3  # o_acc r+w, o_part r, fp16 out; lse r, r, w
+        print(f"merge B={bsz} S={s} H={h} hd={hd}: {ms:.4f} ms  {nbytes / (ms / 1e3) / 1e9:.1f} GB/s")
     else:
         m, d = a.dims
         x = torch.randn(m, d, device=dev)
